@@ -1,0 +1,409 @@
+"""Benchmark of the B200 BF16 GEMM — BASELINE metric: BF16 GEMM TFLOPS at
+M=N=K=4096 and its fraction of the B200 dense BF16 peak; 1/2/4/8-GPU scaling.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one GEMM C = A @ B (A [4096,4096], B [4096,4096] row-major = the
+BASELINE config, U(-1,1) bf16) on each GPU.  With N GPUs (torchrun, one rank
+per GPU) the job is the row-sharded GEMM of the BASELINE: A [4096*N, 4096]
+split into one 4096-row panel per rank, B broadcast once from rank 0 over
+NCCL, C left sharded, so per-GPU work is fixed as N grows ("weak" scaling).
+
+Timing: CUDA events on the launching stream, W warm-up steps, then exactly K
+timed steps bracketed by barrier + synchronize, max over ranks.  Inputs
+rotate over 4 buffer sets (4 x 96 MiB > 126 MB L2) so no step finds its
+operands in L2.  Clocks are sampled through NVML during the timed region.
+
+`e2e` repeats the step through the public API with host (pinned) buffers:
+host->device copy of the step's A (and of B by rank 0, then NCCL broadcast),
+the GEMM, and the device->host copy of C, all inside the timed region.
+
+`--impl reference` times the reference's arithmetic on the host cores (the
+reference has no CPU implementation of its own; this is the oracle port in
+oracle/gemm_oracle.c) on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "cuda-kernels_b200"))
+sys.path.insert(0, REPO)
+
+M_PER_RANK = 4096
+N_DIM = 4096
+K_DIM = 4096
+ROTATE = 4
+FLOPS_PER_STEP = 2.0 * M_PER_RANK * N_DIM * K_DIM
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"burst": float(d["bf16_tflops"]), "sustained": float(d["bf16_tflops_sustained"]),
+                "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"burst": 1590.0, "sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _traffic():
+    """Per-launch DRAM bytes of the GEMM kernel from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "gemm_bf16_4096_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons of one GPU via NVML."""
+
+    def __init__(self, pci_bus_id: str, period_s: float = 0.02):
+        self.period = period_s
+        self.samples = []
+        self._stop = threading.Event()
+        self._thr = None
+        self.error = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_id.encode() if isinstance(pci_bus_id, str) else pci_bus_id)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report, do not fail the bench
+            self.nv = None
+            self.error = repr(e)
+            self.max_mhz = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.samples.append((mhz, reasons, pw))
+            except Exception as e:
+                self.error = repr(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nv is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+
+    def stop(self):
+        if self._thr is not None:
+            self._stop.set()
+            self._thr.join()
+
+    def summary(self):
+        if self.nv is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": len(self.samples),
+                    "error": self.error}
+        nv = self.nv
+        names = {
+            "hw_slowdown": nv.nvmlClocksThrottleReasonHwSlowdown,
+            "hw_thermal_slowdown": nv.nvmlClocksThrottleReasonHwThermalSlowdown,
+            "sw_thermal_slowdown": nv.nvmlClocksThrottleReasonSwThermalSlowdown,
+            "sw_power_cap": nv.nvmlClocksThrottleReasonSwPowerCap,
+            "hw_power_brake_slowdown": nv.nvmlClocksThrottleReasonHwPowerBrakeSlowdown,
+        }
+        seen = sorted({n for _, r, _ in self.samples for n, bit in names.items() if r & bit})
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": seen, "samples": len(self.samples),
+                "power_w_median": round(statistics.median(s[2] for s in self.samples), 1)}
+
+
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(target_s: float = 10.0, rows: int = 512):
+    """The oracle (CPU restatement of the reference arithmetic) on the host
+    cores, on row panels of the same workload, repeated for ~target_s."""
+    import numpy as np
+    from oracle import oracle as o
+    rng = np.random.default_rng(0)
+    a = o.f32_to_bf16(rng.uniform(-1, 1, (rows, K_DIM)).astype(np.float32))
+    b = o.f32_to_bf16(rng.uniform(-1, 1, (K_DIM, N_DIM)).astype(np.float32))
+    o.gemm_f32acc(a[:8], b, 1)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        o.gemm_bf16(a, b, 1)
+        n += 1
+        if time.perf_counter() - t0 >= target_s:
+            break
+    dt = time.perf_counter() - t0
+    tflops = 2.0 * rows * N_DIM * K_DIM * n / dt / 1e12
+    return {"value": round(tflops, 5), "unit": "TFLOPS", "cores": o.num_threads(), "kind": "port",
+            "sample": f"{n} x A[{rows},{K_DIM}] @ B[{K_DIM},{N_DIM}] row panels of the 4096^3 GEMM "
+                      f"(oracle/gemm_oracle.c, fp32 accumulate, {dt:.1f} s)"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference arithmetic on the host cores (oracle port)."""
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import oracle as o
+    rows = args.ref_rows
+    rng = np.random.default_rng(1)
+    a = o.f32_to_bf16(rng.uniform(-1, 1, (rows, K_DIM)).astype(np.float32))
+    b = o.f32_to_bf16(rng.uniform(-1, 1, (K_DIM, N_DIM)).astype(np.float32))
+    for _ in range(args.warmup):
+        o.gemm_bf16(a, b, 1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        o.gemm_bf16(a, b, 1)
+    dt = time.perf_counter() - t0
+    tflops = 2.0 * rows * N_DIM * K_DIM * args.steps / dt / 1e12
+    sample = (f"each step: A[{rows},{K_DIM}] row panel of the 4096^3 GEMM @ B[{K_DIM},{N_DIM}] "
+              f"on {o.num_threads()} host threads (reference has no CPU path; oracle port)")
+    line = {"metric": "bf16_gemm_tflops_4096", "value": round(tflops, 5), "unit": "TFLOPS",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "bf16 gemm M=N=K=4096, A[M,K] x B[K,N] row-major, U(-1,1), fp32 accumulate",
+                       "M": M_PER_RANK, "N": N_DIM, "K": K_DIM, "b_layout": "kn"},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOPS", "cores": o.num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(tflops, 5), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--layout", default="kn", choices=["kn", "nk"])
+    ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-rows", type=int, default=256)
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+    world, rank, local = _dist_setup()
+    import b200_gemm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    M, N, K = M_PER_RANK, N_DIM, K_DIM
+    layout = args.layout
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def rand(shape):
+        return (torch.rand(shape, generator=g, device=dev, dtype=torch.float32) * 2 - 1).to(torch.bfloat16)
+
+    b_shape = (K, N) if layout == "kn" else (N, K)
+    A = [rand((M, K)) for _ in range(ROTATE)]
+    if rank == 0:
+        B = [rand(b_shape) for _ in range(ROTATE)]
+    else:
+        B = [torch.empty(b_shape, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+    C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+
+    # B is broadcast once from rank 0 over NCCL (the BASELINE's row-sharded job).
+    bcast_ms = None
+    if world > 1:
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in B:
+            dist.broadcast(t, src=0)
+        e1.record()
+        torch.cuda.synchronize()
+        bcast_ms = _max_over_ranks(e0.elapsed_time(e1) / ROTATE, world)
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        b200_gemm.gemm(A[i % ROTATE], B[i % ROTATE], b_layout=layout, out=C[i % ROTATE])
+    torch.cuda.synchronize()
+    b200_gemm.check_status()
+
+    props = torch.cuda.get_device_properties(dev)
+    sampler = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    _barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    t_beg.record(stream)
+    for i in range(args.steps):
+        j = i % ROTATE
+        starts[i].record(stream)
+        b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
+        ends[i].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    sampler.stop()
+    b200_gemm.check_status()
+
+    total_ms = _max_over_ranks(t_beg.elapsed_time(t_end), world)
+    launch_ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    launch_ms_max = _max_over_ranks(launch_ms, world)
+    tflops = world * FLOPS_PER_STEP * args.steps / (total_ms / 1e3) / 1e12
+    kernel_tflops = FLOPS_PER_STEP / (launch_ms_max / 1e3) / 1e12
+
+    # cuBLAS on the same GPU, same rotation (context only; not the product).
+    cub_tflops = None
+    if rank == 0:
+        n_cub = min(args.steps, 500)
+        for i in range(10):
+            torch.matmul(A[i % ROTATE], B[i % ROTATE] if layout == "kn" else B[i % ROTATE].t(), out=C[i % ROTATE])
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        c0.record()
+        for i in range(n_cub):
+            j = i % ROTATE
+            torch.matmul(A[j], B[j] if layout == "kn" else B[j].t(), out=C[j])
+        c1.record()
+        torch.cuda.synchronize()
+        cub_tflops = FLOPS_PER_STEP * n_cub / (c0.elapsed_time(c1) / 1e3) / 1e12
+
+    # ---- end to end through the public API with host buffers ----------------
+    e2e = _e2e(args, world, rank, dev, layout, b200_gemm)
+
+    peaks = _peaks()
+    long_region = total_ms >= 500.0
+    peak = peaks["sustained"] if long_region else peaks["burst"]
+    traffic = _traffic()
+    line = {
+        "metric": "bf16_gemm_tflops_4096",
+        "value": round(tflops, 2),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "bf16 gemm M=N=K=4096 per GPU, A[M,K] x B[K,N] row-major, U(-1,1), fp32 accumulate, "
+                               "bf16 out; N>1: A row panels per rank, B broadcast once (NCCL), C sharded",
+                   "M_per_gpu": M, "N": N, "K": K, "b_layout": layout,
+                   "parallelism": f"row-sharded x{world}" if world > 1 else "single",
+                   "l2": f"rotating {ROTATE} input/output sets ({ROTATE * 96} MiB > 126 MB L2)"},
+        "pct_of_peak": round(100.0 * tflops / world / peak, 2),
+        "roofline": {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(kernel_tflops / peak, 4),
+                     "peak_kind": ("sustained" if long_region else "burst") + f" bf16 cuBLAS, {peaks['source']}",
+                     "traffic": (traffic or {}).get("bytes_per_launch"),
+                     "algorithmic_flops_per_launch": FLOPS_PER_STEP,
+                     "avg_launch_ms": round(launch_ms_max, 5)},
+        "clocks": sampler.summary(),
+        "gpu_launches": args.steps,
+        "e2e": e2e,
+        "cublas_same_loop_tflops": round(cub_tflops, 2) if cub_tflops else None,
+        "b_broadcast_ms": round(bcast_ms, 4) if bcast_ms is not None else None,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _e2e(args, world, rank, dev, layout, b200_gemm):
+    """Host buffers -> device -> GEMM -> host, every step, through the public API."""
+    import torch
+    import torch.distributed as dist
+    M, N, K = M_PER_RANK, N_DIM, K_DIM
+    b_shape = (K, N) if layout == "kn" else (N, K)
+    g = torch.Generator().manual_seed(99 + rank)
+    a_h = ((torch.rand((M, K), generator=g) * 2 - 1).to(torch.bfloat16)).pin_memory()
+    b_h = ((torch.rand(b_shape, generator=g) * 2 - 1).to(torch.bfloat16)).pin_memory() if rank == 0 else None
+    c_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    a_d = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    b_d = torch.empty(b_shape, dtype=torch.bfloat16, device=dev)
+    c_d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+    def step():
+        if rank == 0:
+            b_d.copy_(b_h, non_blocking=True)
+        if world > 1:
+            dist.broadcast(b_d, src=0)
+        a_d.copy_(a_h, non_blocking=True)
+        b200_gemm.gemm(a_d, b_d, b_layout=layout, out=c_d)
+        c_h.copy_(c_d, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    tflops = world * FLOPS_PER_STEP * args.e2e_steps / (ms / 1e3) / 1e12
+    h2d = a_h.numel() * 2 + (b_h.numel() * 2 if rank == 0 else 0)
+    return {"value": round(tflops, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": c_h.numel() * 2, "steps": args.e2e_steps,
+            "ms_per_step": round(ms / args.e2e_steps, 4),
+            "path": "pinned host A,B -> H2D -> b200_gemm.gemm (C ABI) -> D2H C, one stream"
+                    + ("; B from rank 0 via NCCL broadcast" if world > 1 else "")}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

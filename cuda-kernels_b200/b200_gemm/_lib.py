@@ -1,0 +1,64 @@
+"""ctypes binding of the C ABI in include/b200_gemm.h.
+
+This is the thin host layer every Python caller (tests, bench, the
+row-sharded driver) goes through.  There is no fallback: if the shared
+library is missing the import of b200_gemm fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from .build import LIB_PATH
+
+B200_OK = 0
+B200_ERR_INVALID_ARG = 1
+B200_ERR_ALIGNMENT = 2
+B200_ERR_UNSUPPORTED_DEVICE = 3
+B200_ERR_CUDA = 4
+B200_ERR_TENSOR_MAP = 5
+B200_ERR_DEVICE_TIMEOUT = 6
+B200_ERR_TOO_LARGE = 7
+
+B200_B_NK = 0
+B200_B_KN = 1
+
+# Every symbol include/b200_gemm.h declares, with its ctypes signature.
+_SIGNATURES = {
+    "b200_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int, ctypes.c_void_p]),
+    "b200_gemm_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "b200_gemm_set_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
+    "b200_gemm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "b200_gemm_version": (ctypes.c_char_p, []),
+}
+
+_lib = None
+
+
+class B200GemmError(RuntimeError):
+    def __init__(self, code: int, what: str = ""):
+        self.code = code
+        msg = load().b200_gemm_strerror(code).decode()
+        super().__init__(f"b200_gemm error {code}: {msg}" + (f" ({what})" if what else ""))
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built; run `python cuda-kernels_b200/b200_gemm/build.py` "
+                              "(or __graft_entry__.build()) first")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)

@@ -1,0 +1,103 @@
+"""Torch-facing operator API of the B200 BF16 GEMM.
+
+`matmul(A, B)` keeps the reference operator's meaning exactly: the
+reference's binding `matmul<fn>(A, B)` (bf16_matmul/matmul.cpp:24-42) takes
+A [M,K] and B stored [N,K] and returns C = A @ B.T (bf16_matmul/README.md:7,
+bf16_matmul/main.py:29-42).  Unlike the reference it reads N from B.size(0)
+(the reference takes B.size(1), matmul.cpp:29, which is only right for square
+shapes), checks dtype/device/layout, and runs on torch's current stream.
+
+`gemm(A, B, b_layout=...)` is the general entry: b_layout "nk" is the
+reference's layout, "kn" is B stored [K,N] row-major (C = A @ B).
+
+Every call goes through the C ABI (include/b200_gemm.h); there is no CPU or
+library fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import B200GemmError
+
+_LAYOUTS = {"nk": _lib.B200_B_NK, "kn": _lib.B200_B_KN}
+
+
+def _check_operand(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if t.stride(1) != 1 and t.numel() > 0:
+        raise ValueError(f"{name} must be row-major (stride(1) == 1), got strides {t.stride()}")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.Tensor | None = None,
+         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """C = A @ op(B) in bf16 with fp32 accumulation on a B200 (sm_100a)."""
+    if b_layout not in _LAYOUTS:
+        raise ValueError(f"b_layout must be 'nk' or 'kn', got {b_layout!r}")
+    _check_operand("A", a)
+    _check_operand("B", b)
+    if a.device != b.device:
+        raise ValueError("A and B must be on the same device")
+    M, K = a.shape
+    if b_layout == "nk":
+        N, Kb = b.shape
+    else:
+        Kb, N = b.shape
+    if Kb != K:
+        raise ValueError(f"inner dimensions differ: A is {tuple(a.shape)}, B ({b_layout}) is {tuple(b.shape)}")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    else:
+        _check_operand("out", out)
+        if tuple(out.shape) != (M, N):
+            raise ValueError(f"out must have shape {(M, N)}, got {tuple(out.shape)}")
+        if out.device != a.device:
+            raise ValueError("out must be on the same device as A")
+    lib = _lib.load()
+    with torch.cuda.device(a.device):
+        s = stream if stream is not None else torch.cuda.current_stream(a.device)
+        rc = lib.b200_gemm_bf16(
+            ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+            M, N, K,
+            max(a.stride(0), 1), max(b.stride(0), 1), max(out.stride(0), 1),
+            _LAYOUTS[b_layout], ctypes.c_void_p(s.cuda_stream))
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc, f"M={M} N={N} K={K} b_layout={b_layout}")
+    return out
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Reference-compatible operator: B is [N,K], returns A @ B.T (bf16_matmul/matmul.cpp:24-42)."""
+    return gemm(a, b, b_layout="nk")
+
+
+def check_status(stream: torch.cuda.Stream | None = None, device: torch.device | int | None = None) -> int:
+    """Synchronise and read/clear the device status word; raises B200GemmError on a device timeout."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        bits = ctypes.c_uint32(0)
+        rc = lib.b200_gemm_status(ctypes.c_void_p(s.cuda_stream), ctypes.byref(bits))
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc, f"device status bits 0x{bits.value:x}")
+    return bits.value
+
+
+def set_timeout_ns(ns: int, device: torch.device | int | None = None) -> None:
+    """Time limit for every device-side wait of later launches on `device` (0 = default 4 s)."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        rc = lib.b200_gemm_set_timeout_ns(int(ns))
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc)

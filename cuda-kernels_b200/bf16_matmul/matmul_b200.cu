@@ -1,0 +1,29 @@
+// matmul_b200.cu — the B200 GEMM as a reference-style MatmulFn launcher.
+//
+// The reference's profiling flow builds `<name>.cu` together with its
+// profile_entry.cpp and calls the C++ function named after the file's
+// basename (scripts/profile.sh:95-123, bf16_matmul/profile_entry.cpp:16-20),
+// with the signature
+//     void(const nv_bfloat16* A, const nv_bfloat16* B, nv_bfloat16* C, int M, int N, int K)
+// (bf16_matmul/profile_entry.cpp:9-14, bf16_matmul/matmul.cpp:5-10).
+//
+// This file is self-contained: it compiles the library sources into the same
+// translation unit, so `CUDA_ARCH=sm_100a scripts/profile.sh bf16_matmul/matmul_b200.cu`
+// (with this file placed beside the reference's profile_entry.cpp) links with no
+// extra flags — the tensor-map encoder is fetched through the runtime, so no
+// -lcuda is needed either.
+//
+// Semantics match the reference launchers: A [M,K] row-major, B [N,K] row-major
+// (C = A * B^T), C [M,N] row-major, legacy default stream, asynchronous.  Where
+// the reference would host-assert (matmul_v8_tuned.cu:238) this accepts any
+// shape; on an argument error it prints the reason to stderr.
+#include <cstdio>
+
+#include <cuda_bf16.h>
+
+#include "../csrc/b200_gemm.cu"
+
+void matmul_b200(const nv_bfloat16* A, const nv_bfloat16* B, nv_bfloat16* C, int M, int N, int K) {
+  const int rc = b200_gemm_bf16(A, B, C, M, N, K, K, K, N, B200_B_NK, nullptr);
+  if (rc != B200_OK) std::fprintf(stderr, "matmul_b200: %s\n", b200_gemm_strerror(rc));
+}

@@ -1,0 +1,201 @@
+// Host side of the C ABI declared in include/b200_gemm.h.
+//
+// Responsibilities: argument checking (the reference only host-asserts tile
+// multiples, bf16_matmul/matmul_v8_tuned.cu:238), TMA descriptor encoding
+// (the reference links -lcuda and calls cuTensorMapEncodeTiled directly,
+// matmul_v8_tuned.cu:181-210; here the driver entry point is fetched through
+// the runtime so nothing links against libcuda), per-device one-time set-up
+// (SM count, shared-memory opt-in, status word), and the persistent launch.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b200_gemm.h"
+#include "gemm_sm100.cuh"
+
+namespace {
+
+// Device status word.  Kernels OR DeviceStatus bits into it when a bounded
+// wait gives up; b200_gemm_status() reads and clears it.
+__device__ uint32_t g_b200_status;
+
+constexpr int kMaxDevices = 64;
+constexpr uint64_t kDefaultTimeoutNs = 4000000000ull;  // 4 s: far above any legitimate wait
+
+// Main-loop configuration of the one kernel instance the library ships today.
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+constexpr int kGroupM = 16;
+
+struct DeviceState {
+  std::once_flag once;
+  int init_rc = B200_OK;
+  int sm_count = 0;
+  uint32_t* status_ptr = nullptr;
+  uint64_t timeout_ns = kDefaultTimeoutNs;
+};
+
+DeviceState g_dev[kMaxDevices];
+
+std::once_flag g_encode_once;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+void load_encode_fn() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess) {
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+}
+
+int init_device(int dev, DeviceState& st) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (major != 10 || minor != 0) return B200_ERR_UNSUPPORTED_DEVICE;
+  if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_b200_status) != cudaSuccess)
+    return B200_ERR_CUDA;
+  auto kern = b200::gemm_bf16_tcgen05_kernel<kBN, kStages>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           b200::SmemPlan<kBN, kStages>::kAllocBytes) != cudaSuccess)
+    return B200_ERR_CUDA;
+  std::call_once(g_encode_once, load_encode_fn);
+  if (g_encode == nullptr) return B200_ERR_CUDA;
+  return B200_OK;
+}
+
+int current_device_state(DeviceState** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return B200_ERR_UNSUPPORTED_DEVICE;
+  DeviceState& st = g_dev[dev];
+  std::call_once(st.once, [&] { st.init_rc = init_device(dev, st); });
+  if (st.init_rc != B200_OK) return st.init_rc;
+  *out = &st;
+  return B200_OK;
+}
+
+// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
+// `pitch_elems` elements between rows, box {box_inner, box_outer}, 128B swizzle.
+int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
+              uint32_t box_inner, uint32_t box_outer, bool is_load) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        is_load ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                              int64_t ldb, int64_t ldc, int b_layout, void* stream_) {
+  if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
+  if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
+  const int64_t kLim = 0x7fffffffLL;
+  if (M > kLim || N > kLim || K > kLim) return B200_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return B200_OK;
+  if (C == nullptr) return B200_ERR_INVALID_ARG;
+  if (ldc < N) return B200_ERR_INVALID_ARG;
+  if (!aligned16(C) || (ldc % 8) != 0) return B200_ERR_ALIGNMENT;
+
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+
+  if (K == 0) {  // empty reduction: C = 0
+    return cudaMemset2DAsync(C, (size_t)ldc * 2, 0, (size_t)N * 2, (size_t)M, stream) == cudaSuccess ? B200_OK
+                                                                                                      : B200_ERR_CUDA;
+  }
+  if (A == nullptr || B == nullptr) return B200_ERR_INVALID_ARG;
+  if (lda < K) return B200_ERR_INVALID_ARG;
+  if (ldb < (b_layout == B200_B_NK ? K : N)) return B200_ERR_INVALID_ARG;
+  if (!aligned16(A) || !aligned16(B) || (lda % 8) != 0 || (ldb % 8) != 0) return B200_ERR_ALIGNMENT;
+
+  CUtensorMap tmA, tmB, tmC;
+  if ((rc = encode_2d(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, b200::kBK, b200::kBM, true)) != B200_OK)
+    return rc;
+  if (b_layout == B200_B_NK) {
+    rc = encode_2d(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, b200::kBK, kBN, true);
+  } else {
+    rc = encode_2d(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, b200::kBK, true);
+  }
+  if (rc != B200_OK) return rc;
+  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, b200::kEpiCols, b200::kEpiRowsPerWarp,
+                      false)) != B200_OK)
+    return rc;
+
+  b200::GemmParams p{};
+  p.M = (int32_t)M;
+  p.N = (int32_t)N;
+  p.K = (int32_t)K;
+  p.num_m_blk = (int32_t)((M + b200::kBM - 1) / b200::kBM);
+  p.num_n_blk = (int32_t)((N + kBN - 1) / kBN);
+  p.num_k_blk = (int32_t)((K + b200::kBK - 1) / b200::kBK);
+  const int64_t tiles = (int64_t)p.num_m_blk * p.num_n_blk;
+  if (tiles > kLim) return B200_ERR_TOO_LARGE;
+  p.num_tiles = (int32_t)tiles;
+  p.group_m = kGroupM;
+  p.b_mn_major = (b_layout == B200_B_KN) ? 1u : 0u;
+  p.timeout_ns = st->timeout_ns;
+  p.status = st->status_ptr;
+
+  const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
+  auto kern = b200::gemm_bf16_tcgen05_kernel<kBN, kStages>;
+  kern<<<grid, b200::kNumThreads, b200::SmemPlan<kBN, kStages>::kAllocBytes, stream>>>(tmA, tmB, tmC, p);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+extern "C" B200_API int b200_gemm_status(void* stream_, uint32_t* device_bits) {
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  uint32_t bits = 0;
+  const uint32_t zero = 0;
+  if (cudaMemcpyAsync(&bits, st->status_ptr, sizeof(bits), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (cudaMemcpyAsync(st->status_ptr, &zero, sizeof(zero), cudaMemcpyHostToDevice, stream) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return B200_ERR_CUDA;
+  if (device_bits != nullptr) *device_bits = bits;
+  return bits == 0 ? B200_OK : B200_ERR_DEVICE_TIMEOUT;
+}
+
+extern "C" B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns) {
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  st->timeout_ns = timeout_ns == 0 ? kDefaultTimeoutNs : timeout_ns;
+  return B200_OK;
+}
+
+extern "C" B200_API const char* b200_gemm_strerror(int code) {
+  switch (code) {
+    case B200_OK: return "ok";
+    case B200_ERR_INVALID_ARG: return "invalid argument";
+    case B200_ERR_ALIGNMENT: return "pointer or row pitch not 16-byte aligned";
+    case B200_ERR_UNSUPPORTED_DEVICE: return "current device is not sm_100 (B200)";
+    case B200_ERR_CUDA: return "CUDA runtime call failed";
+    case B200_ERR_TENSOR_MAP: return "tensor map encode failed";
+    case B200_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case B200_ERR_TOO_LARGE: return "dimension too large";
+    default: return "unknown error";
+  }
+}
+
+extern "C" B200_API const char* b200_gemm_version(void) { return "b200_gemm 0.1.0 sm_100a"; }

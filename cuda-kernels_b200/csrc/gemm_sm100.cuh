@@ -1,0 +1,323 @@
+// Persistent, warp-specialised BF16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   C[M,N] (bf16, row-major) = A[M,K] (bf16, row-major) x B, fp32 accumulate,
+//   B stored either [N,K] row-major ("K-major", the reference's layout:
+//   bf16_matmul/README.md:7, bf16_matmul/matmul_v8_tuned.cu:214) or [K,N]
+//   row-major ("MN-major").
+//
+// This replaces the reference's one-CTA-per-tile mma.sync kernel
+// (bf16_matmul/matmul_v8_tuned.cu:30-179).  The design is Blackwell-first:
+//
+//   warp 0      TMA producer: one lane streams 128B-swizzled A/B K-blocks into
+//               a STAGES-deep shared-memory ring (full/empty mbarriers).
+//   warp 1      MMA issuer: allocates TMEM, one lane issues tcgen05.mma
+//               (M=128, N=BN, K=16) into a double-buffered fp32 accumulator
+//               in TMEM and releases ring stages with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers, round to bf16 (RN),
+//               stage through 128B-swizzled shared memory, TMA-store.  Runs
+//               on accumulator buffer b while the MMA warp fills buffer b^1.
+//
+// Tiles are visited persistently (grid <= #SMs) in grouped order along M so
+// that the tiles in flight at any moment share A row panels and B column
+// panels in L2.  Out-of-range rows/columns/K are handled by TMA: loads fill
+// zeros, stores are clipped, so any M, N, K >= 1 works (row pitches must be
+// multiples of 8 elements for TMA).
+#pragma once
+
+#include <cuda.h>  // CUtensorMap (type only; no driver symbols are linked)
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "ptx_sm100.cuh"
+
+namespace b200 {
+
+constexpr int kBM = 128;          // UMMA M (one CTA)
+constexpr int kBK = 64;           // one 128-byte swizzle row of bf16 per K-block
+constexpr int kUmmaK = 16;        // K per tcgen05.mma kind::f16
+constexpr int kNumThreads = 192;  // 6 warps
+constexpr int kEpiWarps = 4;
+constexpr int kAccBufs = 2;
+constexpr int kTmemCols = 512;
+constexpr int kEpiCols = 64;             // columns per epilogue chunk (one 128B swizzle row of bf16)
+constexpr int kEpiRowsPerWarp = 32;
+constexpr int kEpiBufBytes = kEpiRowsPerWarp * kEpiCols * 2;  // 4 KiB
+
+struct GemmParams {
+  int32_t M, N, K;
+  int32_t num_m_blk, num_n_blk, num_k_blk;
+  int32_t num_tiles;
+  int32_t group_m;       // tiles are rasterised in groups of `group_m` M-blocks
+  uint32_t b_mn_major;   // 0: B is [N,K] (K contiguous); 1: B is [K,N] (N contiguous)
+  uint32_t pad_;
+  uint64_t timeout_ns;   // limit for every mbarrier wait
+  uint32_t* status;      // device status word (DeviceStatus bits), OR-ed on failure
+};
+
+template <int BN, int STAGES>
+struct SmemPlan {
+  static constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
+  static constexpr int kBBytes = BN * kBK * 2;   // 32 KiB for BN=256
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + STAGES * kABytes;
+  static constexpr int kOffC = kOffB + STAGES * kBBytes;
+  static constexpr int kOffBar = kOffC + kEpiWarps * 2 * kEpiBufBytes;
+  // barriers: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
+  static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1;
+  static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
+  static constexpr int kOffAbort = kOffTmemHolder + 4;
+  static constexpr int kBytes = kOffAbort + 4;
+  static constexpr int kAllocBytes = kBytes + 1024;  // slack for 1024-byte alignment
+  static_assert(kAllocBytes <= 232448, "shared memory plan exceeds 227 KiB");
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb, int& nb) {
+  const int tiles_per_group = p.group_m * p.num_n_blk;
+  const int g = t / tiles_per_group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.num_m_blk - first_m, p.group_m);
+  const int r = t - g * tiles_per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ void raise_status(const GemmParams& p, volatile uint32_t* abort_flag, uint32_t code) {
+  *abort_flag = 1u;
+  if (p.status != nullptr) atomicOr(p.status, code);
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using Plan = SmemPlan<BN, STAGES>;
+  static_assert(BN % kEpiCols == 0 && BN >= 64 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static_assert(kAccBufs * BN <= kTmemCols, "accumulators must fit in TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_u32);
+
+  const uint32_t sA = base + Plan::kOffA;
+  const uint32_t sB = base + Plan::kOffB;
+  const uint32_t sC = base + Plan::kOffC;
+  const uint32_t bar0 = base + Plan::kOffBar;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto accf_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + kAccBufs + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 2 * kAccBufs);
+  volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+
+  // ---- set-up -------------------------------------------------------------
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_holder)), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ---- TMA producer -------------------------------------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;  // total K-blocks loaded by this CTA
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        for (int kb = 0; kb < p.num_k_blk; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, Plan::kStageBytes);
+          tma_load_2d(sA + stage * Plan::kABytes, &tmA, fb, kb * kBK, mb * kBM, pol);
+          const uint32_t dstB = sB + stage * Plan::kBBytes;
+          if (p.b_mn_major == 0u) {
+            tma_load_2d(dstB, &tmB, fb, kb * kBK, nb * BN, pol);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_2d(dstB + j * (64 * kBK * 2), &tmB, fb, nb * BN + 64 * j, kb * kBK, pol);
+            }
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) raise_status(p, abort_flag, kDevTimeoutProducer);
+      // Drain: the most recent load into every stage must have landed before
+      // this CTA may exit (its destination is this CTA's shared memory).
+      const uint32_t nst = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+      for (uint32_t i = 0; i < nst; ++i) {
+        const uint32_t it = issued - 1u - i;  // iteration index of a recent load
+        const uint32_t s = it % STAGES;
+        const uint32_t par = (it / STAGES) & 1u;
+        if (!mbar_wait(full_bar(s), par, p.timeout_ns, nullptr)) {
+          raise_status(p, abort_flag, kDevTimeoutDrain);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer ---------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, BN, false, p.b_mn_major != 0u);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_k_blk; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * Plan::kABytes;
+          const uint32_t b0 = sB + stage * Plan::kBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // K-major SW128 operand: rows of 128 bytes, 8-row groups 1024 bytes apart;
+            // the k-th 16-wide K slice starts 32 bytes into each row.
+            const uint64_t ad = smem_desc_sw128(a0 + k * 32, 16, 1024);
+            // MN-major SW128 operand (B as [K,N]): 64-wide N atoms 8 KiB apart (LBO),
+            // 8-row K groups 1024 bytes apart (SBO); the k-th K slice is 16 rows = 2 KiB on.
+            const uint64_t bd = p.b_mn_major ? smem_desc_sw128(b0 + k * 2048, 64 * kBK * 2, 1024)
+                                             : smem_desc_sw128(b0 + k * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));  // stage is free once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(accf_bar(acc));  // accumulator ready for the epilogue
+        if (++acc == kAccBufs) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) raise_status(p, abort_flag, kDevTimeoutMma);
+      // Drain: every MMA issued by this thread must finish before TMEM is freed.
+      umma_commit(drain_bar);
+      if (!mbar_wait(drain_bar, 0u, p.timeout_ns, nullptr)) raise_status(p, abort_flag, kDevTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue (warps 2..5) ----------------------------------------------
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int slot = warp - 2;         // private staging buffers
+    const uint32_t tmem_lane = (uint32_t)(q * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sbuf = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const bool got = mbar_wait(accf_bar(acc), acc_phase, p.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) raise_status(p, abort_flag, kDevTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + tmem_lane + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / kEpiCols; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_row + c * kEpiCols, r0);
+        tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, r1);
+        tmem_ld_wait_regs(r0);
+        tmem_ld_wait_regs(r1);
+        if (c == BN / kEpiCols - 1) {
+          // All TMEM reads of this accumulator are complete: hand it back.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acce_bar(acc));
+        }
+        const uint32_t buf = sC + (uint32_t)((slot * 2 + sbuf) * kEpiBufBytes);
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that used `buf` has read it
+        __syncwarp();
+        const uint32_t row_addr = buf + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* src = (j < 4) ? &r0[j * 8] : &r1[(j - 4) * 8];
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(src[2 * e]), __uint_as_float(src[2 * e + 1]));
+            w[e] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                       "r"(w[3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, nb * BN + c * kEpiCols, mb * kBM + q * kEpiRowsPerWarp);
+          bulk_commit_group();
+        }
+        sbuf ^= 1;
+      }
+      if (++acc == kAccBufs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ---- teardown -------------------------------------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b200

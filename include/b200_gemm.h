@@ -1,0 +1,102 @@
+/*
+ * b200_gemm.h — C ABI of the B200 (sm_100a) BF16 GEMM.
+ *
+ * Drop-in boundary for the reference's `bf16_matmul` operator.  The reference
+ * exposes one C++ host signature per kernel,
+ *
+ *     using MatmulFn = void(const nv_bfloat16* A, const nv_bfloat16* B,
+ *                           nv_bfloat16* C, int M, int N, int K);
+ *
+ * (bf16_matmul/matmul.cpp:5-10, bf16_matmul/profile_entry.cpp:9-14,
+ * bf16_matmul/common.hpp:169-174), implemented by e.g. `matmul_v8_tuned`
+ * (bf16_matmul/matmul_v8_tuned.cu:215-257), and bound to Python by the
+ * template `matmul<fn>` (bf16_matmul/matmul.cpp:24-42).  Those launchers take
+ * raw device pointers, run on the legacy default stream, return nothing and
+ * assert on unsupported shapes.
+ *
+ * This header replaces that surface with a plain C ABI: raw pointers, 64-bit
+ * sizes, an explicit stream, and an integer status instead of a host assert.
+ * No call allocates device memory, throws, or exits the process.
+ *
+ * All functions are thread-safe.  Device memory passed in must belong to the
+ * device that is current on the calling thread.
+ */
+#ifndef B200_GEMM_H_
+#define B200_GEMM_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define B200_OK 0
+#define B200_ERR_INVALID_ARG 1       /* null pointer, negative size, bad layout, ld too small */
+#define B200_ERR_ALIGNMENT 2         /* pointer not 16-byte aligned or row pitch not a multiple of 8 elements */
+#define B200_ERR_UNSUPPORTED_DEVICE 3 /* current device is not compute capability 10.0 (sm_100a) */
+#define B200_ERR_CUDA 4              /* a CUDA runtime call (launch, attribute, entry point) failed */
+#define B200_ERR_TENSOR_MAP 5        /* cuTensorMapEncodeTiled rejected a descriptor */
+#define B200_ERR_DEVICE_TIMEOUT 6    /* a kernel wait hit its time limit (see b200_gemm_status) */
+#define B200_ERR_TOO_LARGE 7         /* a dimension exceeds 2^31-1 */
+
+/* Layout of the B operand. */
+#define B200_B_NK 0 /* B stored [N,K] row-major (K contiguous): C = A * B^T.  The reference's layout. */
+#define B200_B_KN 1 /* B stored [K,N] row-major (N contiguous): C = A * B. */
+
+/*
+ * C[M,N] = A[M,K] * op(B), bf16 inputs, fp32 accumulation, bf16 output
+ * rounded to nearest-even.
+ *
+ *   A       device pointer, bf16, row-major [M, lda >= K]
+ *   B       device pointer, bf16, [N, ldb >= K] if b_layout == B200_B_NK,
+ *                                 [K, ldb >= N] if b_layout == B200_B_KN
+ *   C       device pointer, bf16, row-major [M, ldc >= N]; fully overwritten
+ *   M,N,K   any values >= 0 (M==0 or N==0: no-op; K==0: C is zero-filled)
+ *   lda/ldb/ldc  row pitches in elements, multiples of 8 (TMA needs 16-byte pitches)
+ *   stream  cudaStream_t to run on (NULL = legacy default stream)
+ *
+ * Asynchronous: returns after the launch.  Launch-time problems are returned
+ * directly; a device-side wait that times out is reported by
+ * b200_gemm_status().
+ *
+ * Replaces: matmul_v8_tuned (bf16_matmul/matmul_v8_tuned.cu:215-257) called
+ * through MatmulFn (bf16_matmul/matmul.cpp:5-10); with b_layout = B200_B_NK,
+ * lda = ldb = K, ldc = N and the default stream it computes the same product.
+ */
+B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                   int64_t ldb, int64_t ldc, int b_layout, void* stream);
+
+/*
+ * Waits for `stream`, then reads and clears the current device's status word.
+ * Returns B200_OK, B200_ERR_DEVICE_TIMEOUT (a kernel gave up on a wait; the
+ * raw bits are stored to *device_bits if non-NULL), or B200_ERR_CUDA.
+ * The reference has no error reporting at all (host assert only,
+ * bf16_matmul/matmul_v8_tuned.cu:238).
+ */
+B200_API int b200_gemm_status(void* stream, uint32_t* device_bits);
+
+/*
+ * Sets the time limit, in nanoseconds, that every device-side wait of later
+ * launches on this device gets (default 4e9 ns).  0 restores the default.
+ * No reference counterpart (its waits are unbounded, bf16_matmul/common.hpp:128-145).
+ */
+B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns);
+
+/* Static text for a return code. */
+B200_API const char* b200_gemm_strerror(int code);
+
+/* Library version, e.g. "b200_gemm 0.1.0 sm_100a". */
+B200_API const char* b200_gemm_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* B200_GEMM_H_ */

@@ -1,0 +1,142 @@
+"""ctypes wrapper of oracle/gemm_oracle.c (CPU restatement of the reference's
+BF16 GEMM: bf16 inputs, fp32 accumulation in K=16 partial sums, RN-even bf16
+output; see the header of gemm_oracle.c for the reference lines it follows).
+
+TEST INFRASTRUCTURE ONLY — imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU baseline, never by the product path.
+
+Arrays are numpy: bf16 values travel as their uint16 bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_v8_tuned.so")
+
+_lib = None
+_ref = None
+
+
+def build() -> None:
+    """Compile the C oracle (gcc) and, when the reference checkout is present, oracle/_ref."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        src = os.path.join(HERE, "gemm_oracle.c")
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+            subprocess.run(["make", "-s", "-C", HERE], check=True)
+        lib = ctypes.CDLL(LIB_PATH)
+        i64 = ctypes.c_int64
+        vp = ctypes.c_void_p
+        lib.oracle_gemm_bf16_f32acc.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
+        lib.oracle_gemm_bf16.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
+        lib.oracle_gemm_bf16_f64.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
+        lib.oracle_f32_to_bf16.argtypes = [vp, vp, i64]
+        lib.oracle_bf16_to_f32.argtypes = [vp, vp, i64]
+        for f in (lib.oracle_gemm_bf16_f32acc, lib.oracle_gemm_bf16, lib.oracle_gemm_bf16_f64):
+            f.restype = ctypes.c_int
+        lib.oracle_num_threads.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+def _u16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    if x.dtype != np.uint16:
+        raise TypeError(f"expected uint16 bf16 bit patterns, got {x.dtype}")
+    return x
+
+
+def _dims(a: np.ndarray, b: np.ndarray, b_layout: int):
+    M, K = a.shape
+    if b_layout == 0:
+        N, Kb = b.shape
+    else:
+        Kb, N = b.shape
+    if Kb != K:
+        raise ValueError(f"inner dims differ: {a.shape} vs {b.shape} (layout {b_layout})")
+    return M, N, K
+
+
+def num_threads() -> int:
+    return int(_load().oracle_num_threads())
+
+
+def gemm_f32acc(a: np.ndarray, b: np.ndarray, b_layout: int = 0, threads: int = 0) -> np.ndarray:
+    """fp32 result (before bf16 rounding) of A @ op(B); b_layout 0: B is [N,K], 1: B is [K,N]."""
+    a, b = _u16(a), _u16(b)
+    M, N, K = _dims(a, b, b_layout)
+    c = np.empty((M, N), dtype=np.float32)
+    rc = _load().oracle_gemm_bf16_f32acc(a.ctypes.data, b.ctypes.data, c.ctypes.data, M, N, K,
+                                         max(K, 1), b.shape[1] if b.size else 1, max(N, 1), b_layout, threads)
+    if rc != 0:
+        raise RuntimeError("oracle_gemm_bf16_f32acc failed")
+    return c
+
+
+def gemm_bf16(a: np.ndarray, b: np.ndarray, b_layout: int = 0, threads: int = 0) -> np.ndarray:
+    """bf16 bit patterns of RN(A @ op(B)) with fp32 accumulation — what the reference kernel outputs."""
+    a, b = _u16(a), _u16(b)
+    M, N, K = _dims(a, b, b_layout)
+    c = np.empty((M, N), dtype=np.uint16)
+    rc = _load().oracle_gemm_bf16(a.ctypes.data, b.ctypes.data, c.ctypes.data, M, N, K,
+                                  max(K, 1), b.shape[1] if b.size else 1, max(N, 1), b_layout, threads)
+    if rc != 0:
+        raise RuntimeError("oracle_gemm_bf16 failed")
+    return c
+
+
+def gemm_f64(a: np.ndarray, b: np.ndarray, b_layout: int = 0, threads: int = 0):
+    """(near-exact fp64 product, fp64 sum of |a*b|) of A @ op(B)."""
+    a, b = _u16(a), _u16(b)
+    M, N, K = _dims(a, b, b_layout)
+    c = np.empty((M, N), dtype=np.float64)
+    s = np.empty((M, N), dtype=np.float64)
+    rc = _load().oracle_gemm_bf16_f64(a.ctypes.data, b.ctypes.data, c.ctypes.data, s.ctypes.data, M, N, K,
+                                      max(K, 1), b.shape[1] if b.size else 1, b_layout, threads)
+    if rc != 0:
+        raise RuntimeError("oracle_gemm_bf16_f64 failed")
+    return c, s
+
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, dtype=np.uint16)
+    _load().oracle_f32_to_bf16(x.ctypes.data, y.ctypes.data, x.size)
+    return y
+
+
+def bf16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = _u16(x)
+    y = np.empty(x.shape, dtype=np.float32)
+    _load().oracle_bf16_to_f32(x.ctypes.data, y.ctypes.data, x.size)
+    return y
+
+
+# --- the reference's own kernel (oracle/_ref), GPU only ---------------------
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB_PATH)
+
+
+def ref_lib():
+    """ctypes handle of oracle/_ref/libref_v8_tuned.so: the reference's matmul_v8_tuned
+    (bf16_matmul/matmul_v8_tuned.cu:215-257) rebuilt for sm_100a."""
+    global _ref
+    if _ref is None:
+        lib = ctypes.CDLL(REF_LIB_PATH)
+        lib.ref_matmul_v8_tuned.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        lib.ref_matmul_v8_tuned.restype = ctypes.c_int
+        _ref = lib
+    return _ref

@@ -1,0 +1,72 @@
+"""CPU tests of the C-ABI library: it loads, exports every symbol that
+include/b200_gemm.h declares, and rejects bad arguments before touching the
+GPU (these calls return from the argument checks; no kernel is launched)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "b200_gemm.h")
+
+
+def _declared():
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"B200_API\s+(?:const\s+)?\w+\*?\s+\*?(b200_\w+)\s*\(", txt)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "b200_gemm_bf16" in names and "b200_gemm_status" in names
+    assert len(names) >= 5
+
+
+def test_library_exports_every_declared_symbol():
+    from b200_gemm import _lib
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in include/b200_gemm.h but not exported"
+    assert set(_declared()) <= set(_lib.exported_symbols())
+
+
+def test_version_and_strerror():
+    from b200_gemm import _lib
+    lib = _lib.load()
+    assert b"sm_100a" in lib.b200_gemm_version()
+    assert lib.b200_gemm_strerror(0) == b"ok"
+    assert lib.b200_gemm_strerror(6).startswith(b"device-side wait")
+    assert lib.b200_gemm_strerror(999) == b"unknown error"
+
+
+def test_argument_errors_without_gpu():
+    from b200_gemm import _lib
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    fake = P(0x10000)  # never dereferenced: every call below fails its host-side checks first
+    # negative size
+    assert lib.b200_gemm_bf16(fake, fake, fake, -1, 8, 8, 8, 8, 8, 0, None) == _lib.B200_ERR_INVALID_ARG
+    # bad layout
+    assert lib.b200_gemm_bf16(fake, fake, fake, 8, 8, 8, 8, 8, 8, 7, None) == _lib.B200_ERR_INVALID_ARG
+    # empty output is a no-op
+    assert lib.b200_gemm_bf16(fake, fake, fake, 0, 8, 8, 8, 8, 8, 0, None) == _lib.B200_OK
+    assert lib.b200_gemm_bf16(fake, fake, fake, 8, 0, 8, 8, 8, 8, 0, None) == _lib.B200_OK
+    # null C
+    assert lib.b200_gemm_bf16(fake, fake, None, 8, 8, 8, 8, 8, 8, 0, None) == _lib.B200_ERR_INVALID_ARG
+    # ldc < N
+    assert lib.b200_gemm_bf16(fake, fake, fake, 8, 16, 8, 8, 8, 8, 0, None) == _lib.B200_ERR_INVALID_ARG
+    # misaligned C / pitch not a multiple of 8 elements
+    assert lib.b200_gemm_bf16(fake, fake, P(0x10002), 8, 8, 8, 8, 8, 8, 0, None) == _lib.B200_ERR_ALIGNMENT
+    assert lib.b200_gemm_bf16(fake, fake, fake, 8, 6, 8, 8, 8, 6, 0, None) == _lib.B200_ERR_ALIGNMENT
+    # too large
+    assert lib.b200_gemm_bf16(fake, fake, fake, 1 << 31, 8, 8, 8, 8, 8, 0, None) == _lib.B200_ERR_TOO_LARGE
+
+
+def test_product_path_does_not_touch_oracle():
+    """The package must not import or load anything under oracle/."""
+    pkg = os.path.join(REPO, "cuda-kernels_b200")
+    for root, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
+                txt = open(os.path.join(root, f), errors="ignore").read()
+                assert "oracle" not in re.sub(r"#.*|//.*", "", txt).lower() or f == "build.py", f

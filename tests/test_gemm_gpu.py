@@ -1,0 +1,198 @@
+"""GPU parity tests of the B200 GEMM, called through the C ABI (b200_gemm.gemm
+wraps b200_gemm_bf16 via ctypes), against:
+  * the CPU oracle (oracle/gemm_oracle.c) and its fp64 product,
+  * the reference's own matmul_v8_tuned rebuilt for sm_100a (oracle/_ref),
+  * cuBLAS (torch.matmul), the check the reference's main.py makes
+    (bf16_matmul/main.py:44-54).
+Tolerances are stated in tests/_util.py (check_parity).
+"""
+import numpy as np
+import pytest
+import torch
+
+import b200_gemm
+from oracle import oracle as o
+from tests._util import bits, check_parity, normal_bf16, uniform_bf16
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _pad8(x: int) -> int:
+    return max((x + 7) // 8 * 8, 8)
+
+
+def _padded(t: torch.Tensor) -> torch.Tensor:
+    """Device copy of a 2-D bf16 tensor with its row pitch rounded up to 8 elements."""
+    r, c = t.shape
+    buf = torch.zeros((r, _pad8(c)), dtype=torch.bfloat16, device=DEV)
+    buf[:, :c] = t.to(DEV)
+    return buf[:, :c]
+
+
+def _run(a, b, layout):
+    """Run the GPU GEMM on padded device copies; returns the bf16 result on the CPU."""
+    ad, bd = _padded(a), _padded(b)
+    M = a.shape[0]
+    N = b.shape[0] if layout == "nk" else b.shape[1]
+    out = torch.full((M, _pad8(N)), float("nan"), dtype=torch.bfloat16, device=DEV)[:, :N]
+    res = b200_gemm.gemm(ad, bd, b_layout=layout, out=out)
+    assert res.data_ptr() == out.data_ptr()
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    return out.cpu()
+
+
+def _make(M, N, K, layout, seed, dist="uniform"):
+    gen = uniform_bf16 if dist == "uniform" else normal_bf16
+    a = gen((M, K), seed)
+    b_nk = gen((N, K), seed + 7)
+    b = b_nk if layout == "nk" else b_nk.t().contiguous()
+    return a, b, b_nk
+
+
+EDGE_SHAPES = [
+    (1, 1, 1), (1, 8, 8), (5, 3, 7), (8, 8, 8), (16, 24, 40), (128, 256, 64), (127, 255, 63),
+    (129, 257, 65), (128, 64, 128), (200, 300, 136), (256, 512, 192), (300, 600, 200),
+    (1000, 72, 40), (64, 100, 1000), (131, 517, 333),
+]
+
+
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("shape", EDGE_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_edge_shapes_vs_oracle(shape, layout):
+    M, N, K = shape
+    a, b, b_nk = _make(M, N, K, layout, seed=M * 7919 + N * 31 + K)
+    c = _run(a, b, layout)
+    c_or = o.gemm_bf16(bits(a), bits(b_nk), 0)
+    c64, _ = o.gemm_f64(bits(a), bits(b_nk), 0)
+    check_parity(bits(c), c64, c_or, ctx=f"{shape} {layout}")
+
+
+def _sampled_parity(a, b_nk, c, rows, ctx):
+    a_s = bits(a[rows])
+    c_or = o.gemm_bf16(a_s, bits(b_nk), 0)
+    c64, _ = o.gemm_f64(a_s, bits(b_nk), 0)
+    return check_parity(bits(c[rows]), c64, c_or, ctx=ctx)
+
+
+def _rows(M, n, seed):
+    rng = np.random.default_rng(seed)
+    r = set(rng.choice(M, size=min(n, M), replace=False).tolist()) | {0, M - 1}
+    return torch.tensor(sorted(r))
+
+
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("shape", [(2048, 4096, 128), (4096, 4096, 64), (1024, 1024, 8192), (640, 2560, 520)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_persistent_multi_tile_vs_oracle(shape, layout):
+    """More tiles than SMs (each CTA loops over several tiles, both TMEM
+    accumulator buffers and every ring stage wrap), checked on sampled rows."""
+    M, N, K = shape
+    a, b, b_nk = _make(M, N, K, layout, seed=K + N)
+    c = _run(a, b, layout)
+    _sampled_parity(a, b_nk, c, _rows(M, 48, M + K), ctx=f"{shape} {layout}")
+
+
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_headline_4096_full_oracle(layout):
+    """M=N=K=4096, U(-1,1) bf16, every element against the oracle."""
+    M = N = K = 4096
+    a, b, b_nk = _make(M, N, K, layout, seed=4096)
+    c = _run(a, b, layout)
+    c_or = o.gemm_bf16(bits(a), bits(b_nk), 0)
+    c32 = o.gemm_f32acc(bits(a), bits(b_nk), 0).astype(np.float64)
+    check_parity(bits(c), c32, c_or, ctx=f"4096^3 {layout}")
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (256, 128, 192), (1024, 2048, 512), (8192, 4096, 1024)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_vs_reference_kernel(shape):
+    """Same seeded inputs through the reference's matmul_v8_tuned (sm_100a rebuild)."""
+    if not o.ref_available():
+        pytest.skip("oracle/_ref/libref_v8_tuned.so not built")
+    M, N, K = shape
+    a = normal_bf16((M, K), 5).to(DEV)
+    b = normal_bf16((N, K), 6).to(DEV)
+    c_ref = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    torch.cuda.synchronize()
+    assert o.ref_lib().ref_matmul_v8_tuned(a.data_ptr(), b.data_ptr(), c_ref.data_ptr(), M, N, K) == 0
+    torch.cuda.synchronize()
+    c = b200_gemm.matmul(a, b)
+    torch.cuda.synchronize()
+    cb, rb = bits(c), bits(c_ref)
+    x = (cb.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    y = (rb.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    from tests._util import bf16_ulp
+    d = np.abs(x - y) / bf16_ulp(np.maximum(np.abs(y), np.sqrt(np.mean(y ** 2)) * 2 ** -8))
+    assert d.max() <= 1.0, f"max {d.max():.2f} ulp from matmul_v8_tuned"
+    assert np.mean(cb != rb) < 0.01
+
+
+def test_vs_cublas_like_reference_main():
+    """The reference's own correctness gate: assert_close against torch.matmul
+    with default bf16 tolerances on N(0,1) 4096x4096 inputs (bf16_matmul/main.py:27-54)."""
+    a = torch.randn((4096, 4096), dtype=torch.bfloat16, generator=torch.Generator().manual_seed(1)).to(DEV)
+    b = torch.randn((4096, 4096), dtype=torch.bfloat16, generator=torch.Generator().manual_seed(2)).to(DEV)
+    ref = torch.matmul(a, b.transpose(0, 1).contiguous())
+    out = b200_gemm.matmul(a, b)
+    torch.testing.assert_close(out, ref)
+    out_kn = b200_gemm.gemm(a, b.transpose(0, 1).contiguous(), b_layout="kn")
+    torch.testing.assert_close(out_kn, ref)
+
+
+def test_torch_binding_matches_c_abi():
+    from b200_gemm.binding import load_binding
+    ext = load_binding()
+    a = uniform_bf16((300, 520), 1).to(DEV)
+    b = uniform_bf16((200, 520), 2).to(DEV)
+    c1 = ext.matmul_b200(a, b)
+    c2 = b200_gemm.matmul(a, b)
+    c3 = ext.matmul_b200_kn(a, b.t().contiguous())
+    torch.cuda.synchronize()
+    assert c1.shape == (300, 200)  # N from B.size(0), unlike the reference's B.size(1)
+    assert torch.equal(c1, c2) and torch.equal(c1, c3)
+    with pytest.raises(RuntimeError):
+        ext.matmul_b200(a.float(), b)
+    with pytest.raises(RuntimeError):
+        ext.matmul_b200(a, b[:, :100])
+
+
+def test_k_zero_m_zero_and_streams():
+    a = torch.empty((64, 0), dtype=torch.bfloat16, device=DEV)
+    b = torch.empty((32, 0), dtype=torch.bfloat16, device=DEV)
+    c = torch.full((64, 32), 3.0, dtype=torch.bfloat16, device=DEV)
+    b200_gemm.gemm(a, b, out=c)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(c) == 0
+    e = b200_gemm.gemm(torch.empty((0, 16), dtype=torch.bfloat16, device=DEV),
+                       torch.ones((8, 16), dtype=torch.bfloat16, device=DEV))
+    assert e.shape == (0, 8)
+    # a side stream: result must be ready after synchronising that stream only
+    s = torch.cuda.Stream()
+    a = uniform_bf16((512, 256), 3).to(DEV)
+    b = uniform_bf16((384, 256), 4).to(DEV)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        c = b200_gemm.matmul(a, b)
+    s.synchronize()
+    ref = o.gemm_bf16(bits(a.cpu()), bits(b.cpu()), 0)
+    assert np.mean(bits(c) != ref) < 0.01
+
+
+def test_strided_views_and_errors():
+    base = uniform_bf16((256, 640), 9).to(DEV)
+    a = base[:, 64:64 + 320]  # lda = 640, offset 128 bytes
+    b = uniform_bf16((96, 320), 10).to(DEV)
+    out_buf = torch.zeros((256, 200), dtype=torch.bfloat16, device=DEV)
+    out = out_buf[:, 8:8 + 96]
+    b200_gemm.gemm(a, b, out=out)
+    torch.cuda.synchronize()
+    ref = o.gemm_bf16(bits(a.cpu()), bits(b.cpu()), 0)
+    assert np.mean(bits(out) != ref) < 0.01
+    assert torch.count_nonzero(out_buf[:, :8]) == 0 and torch.count_nonzero(out_buf[:, 104:]) == 0
+    with pytest.raises(b200_gemm.B200GemmError):
+        b200_gemm.gemm(base[:, 1:321], b)  # 2-byte offset: not 16-byte aligned
+    with pytest.raises(ValueError):
+        b200_gemm.gemm(a, b.t())  # not row-major

@@ -1,0 +1,81 @@
+"""CPU tests of the oracle (gemm_oracle.c): rounding known answers, internal
+consistency, accuracy against an fp64 product, and the pin against outputs
+of the reference's own kernel (tests/golden/)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as o
+from tests._util import bf16_bits_to_f64, check_parity
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_bf16_rounding_known_answers():
+    # Values chosen on and around bf16 rounding boundaries (8 significant bits).
+    x = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, 1.0 + 2 ** -8 + 2 ** -20, -1.0 - 2 ** -8,
+                  3.0e38, 0.0, -0.0, 2 ** -130, np.inf, -np.inf], dtype=np.float32)
+    want = np.array([0x3F80, 0x3F80, 0x3F82, 0x3F81, 0xBF80, 0x7F62, 0x0000, 0x8000, 0x0008, 0x7F80, 0xFF80],
+                    dtype=np.uint16)
+    got = o.f32_to_bf16(x)
+    assert np.array_equal(got, want), [hex(v) for v in got]
+    assert o.f32_to_bf16(np.array([np.nan], dtype=np.float32))[0] == 0x7FFF
+    back = o.bf16_to_f32(want[:5])
+    assert back.tolist() == [1.0, 1.0, 1.0 + 2 ** -6, 1.0 + 2 ** -7, -1.0]
+
+
+def test_tiny_known_product():
+    # 2x3 @ (2x3)^T with exactly representable values.
+    a = o.f32_to_bf16(np.array([[1, 2, 3], [-1, 0.5, 4]], dtype=np.float32))
+    b = o.f32_to_bf16(np.array([[1, 1, 1], [2, -1, 0.25]], dtype=np.float32))
+    c = o.gemm_f32acc(a, b, 0)
+    assert c.tolist() == [[6.0, 0.75], [3.5, -1.5]]
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (3, 5, 7), (17, 33, 40), (64, 80, 129), (130, 70, 300)])
+def test_layouts_agree_and_match_fp64(shape):
+    M, N, K = shape
+    rng = np.random.default_rng(M * 1000 + N * 10 + K)
+    a = o.f32_to_bf16(rng.uniform(-1, 1, (M, K)).astype(np.float32))
+    b = o.f32_to_bf16(rng.uniform(-1, 1, (N, K)).astype(np.float32))
+    c_nk = o.gemm_bf16(a, b, 0)
+    c_kn = o.gemm_bf16(a, np.ascontiguousarray(b.T), 1)
+    assert np.array_equal(c_nk, c_kn)
+    c64, sabs = o.gemm_f64(a, b, 0)
+    c32 = o.gemm_f32acc(a, b, 0)
+    # fp32 accumulation error is bounded by ~K * 2^-24 * sum|a*b|.
+    assert np.all(np.abs(c32 - c64) <= K * 2.0 ** -24 * sabs + 1e-30)
+    check_parity(c_nk, c64, c_nk, ctx=str(shape))
+
+
+def test_k_zero_and_empty():
+    a = np.zeros((4, 0), dtype=np.uint16)
+    b = np.zeros((3, 0), dtype=np.uint16)
+    assert np.array_equal(o.gemm_f32acc(a, b, 0), np.zeros((4, 3), np.float32))
+    assert o.gemm_bf16(np.zeros((0, 8), np.uint16), np.zeros((5, 8), np.uint16), 0).shape == (0, 5)
+
+
+def _golden_files():
+    return sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+
+
+def test_golden_fixtures_present():
+    assert _golden_files(), "tests/golden/*.npz missing (made by tests/golden/make_golden.py on a B200)"
+
+
+@pytest.mark.parametrize("path", _golden_files(), ids=lambda p: os.path.basename(p))
+def test_oracle_matches_reference_kernel_outputs(path):
+    """Pin: the CPU restatement reproduces what the reference's matmul_v8_tuned
+    (compiled for sm_100a from its own sources) produced on a B200."""
+    z = np.load(path)
+    a, b, c_ref = z["A"], z["B"], z["C_ref_v8_tuned"]
+    c_or = o.gemm_bf16(a, b, 0)
+    c64, _ = o.gemm_f64(a, b, 0)
+    stats = check_parity(c_ref, c64, c_or, ctx=os.path.basename(path))
+    # The reference and the oracle round the same fp32-accumulated value; they may
+    # only disagree where summation order moves a value across a rounding boundary.
+    assert stats["frac_diff"] < 0.01
+    if "C_cublas" in z.files:
+        check_parity(z["C_cublas"], c64, c_or, ctx=os.path.basename(path) + " cublas")
