@@ -218,12 +218,14 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layout", default="kn", choices=["kn", "nk"])
     ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--cublas-steps", type=int, default=500, help="cuBLAS comparison loop length (0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-rows", type=int, default=256)
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
+    args.e2e_steps = max(args.e2e_steps, 1)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -299,8 +301,8 @@ def main(argv=None) -> int:
 
     # cuBLAS on the same GPU, same rotation (context only; not the product).
     cub_tflops = None
-    if rank == 0:
-        n_cub = min(args.steps, 500)
+    if rank == 0 and args.cublas_steps > 0:
+        n_cub = args.cublas_steps
         for i in range(10):
             torch.matmul(A[i % ROTATE], B[i % ROTATE] if layout == "kn" else B[i % ROTATE].t(), out=C[i % ROTATE])
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -5,42 +5,54 @@
 // Differences from the reference binding, all deliberate:
 //   * N comes from B.size(0) for the reference's [N,K] B (the reference reads
 //     B.size(1), matmul.cpp:29, which is K; only square shapes worked);
-//   * dtype, device, rank and row-major layout are checked (TORCH_CHECK)
-//     instead of assumed;
+//   * dtype, device, rank and row-major layout are checked instead of assumed;
 //   * the kernel runs on torch's current CUDA stream, not the legacy stream;
 //   * launch errors raise instead of being ignored.
 // The product is computed by the C ABI entry point b200_gemm_bf16
 // (include/b200_gemm.h); this file only adapts torch tensors to it.
+//
+// Errors are raised as standard C++ exceptions, which pybind11 turns into
+// Python ValueError (std::invalid_argument) and RuntimeError
+// (std::runtime_error).  TORCH_CHECK is not used: with the torch 2.11 build in
+// this image, a TORCH_CHECK whose message contains an integer crashes the
+// process inside an extension module instead of raising.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+
+#include <stdexcept>
+#include <string>
 
 #include "b200_gemm.h"
 
 namespace {
 
+[[noreturn]] void bad_arg(const std::string& msg) { throw std::invalid_argument(msg); }
+
 void check_operand(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16");
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
-  TORCH_CHECK(t.numel() == 0 || t.stride(1) == 1, name, " must be row-major");
+  if (t.scalar_type() != torch::kBFloat16) bad_arg(std::string(name) + " must be bfloat16");
+  if (!t.is_cuda()) bad_arg(std::string(name) + " must be a CUDA tensor");
+  if (t.dim() != 2) bad_arg(std::string(name) + " must be 2-D");
+  if (t.numel() != 0 && t.stride(1) != 1) bad_arg(std::string(name) + " must be row-major");
 }
 
 torch::Tensor run(const torch::Tensor& A, const torch::Tensor& B, int b_layout) {
   check_operand(A, "A");
   check_operand(B, "B");
-  TORCH_CHECK(A.device() == B.device(), "A and B must be on the same device");
+  if (A.device() != B.device()) bad_arg("A and B must be on the same device");
   const int64_t M = A.size(0);
   const int64_t K = A.size(1);
   const int64_t N = (b_layout == B200_B_NK) ? B.size(0) : B.size(1);
   const int64_t Kb = (b_layout == B200_B_NK) ? B.size(1) : B.size(0);
-  TORCH_CHECK(Kb == K, "inner dimensions differ: A is [", M, ",", K, "], B gives K=", Kb);
+  if (Kb != K)
+    bad_arg("inner dimensions differ: A is [" + std::to_string(M) + "," + std::to_string(K) + "], B gives K=" +
+            std::to_string(Kb));
   const c10::cuda::CUDAGuard guard(A.device());
   auto C = torch::empty({M, N}, A.options());
   const int rc = b200_gemm_bf16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, std::max<int64_t>(A.stride(0), 1),
                                 std::max<int64_t>(B.stride(0), 1), std::max<int64_t>(C.stride(0), 1), b_layout,
                                 at::cuda::getCurrentCUDAStream(A.device().index()).stream());
-  TORCH_CHECK(rc == B200_OK, "b200_gemm_bf16 failed: ", b200_gemm_strerror(rc));
+  if (rc != B200_OK) throw std::runtime_error(std::string("b200_gemm_bf16 failed: ") + b200_gemm_strerror(rc));
   return C;
 }
 

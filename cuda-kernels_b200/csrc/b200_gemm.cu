@@ -16,6 +16,7 @@
 
 #include "../../include/b200_gemm.h"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_pair.cuh"
 
 namespace {
 
@@ -26,15 +27,20 @@ __device__ uint32_t g_b200_status;
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kDefaultTimeoutNs = 4000000000ull;  // 4 s: far above any legitimate wait
 
-// Main-loop configuration of the one kernel instance the library ships today.
+// Kernel configurations shipped by the library.
+//   single: one CTA per 128 x 256 tile, 4-stage ring   (M <= 128)
+//   pair:   a CTA pair per 256 x 256 tile, 6-stage ring (everything else)
 constexpr int kBN = 256;
 constexpr int kStages = 4;
+constexpr int kPairBN = 256;
+constexpr int kPairStages = 6;
 constexpr int kGroupM = 16;
 
 struct DeviceState {
   std::once_flag once;
   int init_rc = B200_OK;
   int sm_count = 0;
+  int max_pairs = 0;  // co-resident 2-CTA clusters of the pair kernel
   uint32_t* status_ptr = nullptr;
   uint64_t timeout_ns = kDefaultTimeoutNs;
 };
@@ -62,10 +68,34 @@ int init_device(int dev, DeviceState& st) {
   if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return B200_ERR_CUDA;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_b200_status) != cudaSuccess)
     return B200_ERR_CUDA;
-  auto kern = b200::gemm_bf16_tcgen05_kernel<kBN, kStages>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           b200::SmemPlan<kBN, kStages>::kAllocBytes) != cudaSuccess)
+  constexpr int single_smem = b200::SmemPlan<kBN, kStages>::kAllocBytes;
+  constexpr int pair_smem = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
+  if (cudaFuncSetAttribute(b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, single_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, single_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess)
     return B200_ERR_CUDA;
+  auto pkern = b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (st.sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
+    cfg.dynamicSmemBytes = pair_smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, pkern, &cfg) != cudaSuccess || clusters <= 0) return B200_ERR_CUDA;
+    st.max_pairs = clusters;
+  }
   std::call_once(g_encode_once, load_encode_fn);
   if (g_encode == nullptr) return B200_ERR_CUDA;
   return B200_OK;
@@ -126,11 +156,17 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
   if (ldb < (b_layout == B200_B_NK ? K : N)) return B200_ERR_INVALID_ARG;
   if (!aligned16(A) || !aligned16(B) || (lda % 8) != 0 || (ldb % 8) != 0) return B200_ERR_ALIGNMENT;
 
+  // M <= 128 fits one 128-row tile per column block: the single-CTA kernel.
+  // Larger M uses CTA pairs (256-row tiles).
+  const bool use_pair = M > b200::kBM;
+  const uint32_t bn = use_pair ? (uint32_t)kPairBN : (uint32_t)kBN;
+  const uint32_t b_rows = use_pair ? bn / 2 : bn;  // B rows (K-major) one CTA loads per K-block
+
   CUtensorMap tmA, tmB, tmC;
   if ((rc = encode_2d(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, b200::kBK, b200::kBM, true)) != B200_OK)
     return rc;
   if (b_layout == B200_B_NK) {
-    rc = encode_2d(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, b200::kBK, kBN, true);
+    rc = encode_2d(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, b200::kBK, b_rows, true);
   } else {
     rc = encode_2d(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, b200::kBK, true);
   }
@@ -139,12 +175,13 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
                       false)) != B200_OK)
     return rc;
 
+  const int64_t bm = use_pair ? b200::kPairBM : b200::kBM;
   b200::GemmParams p{};
   p.M = (int32_t)M;
   p.N = (int32_t)N;
   p.K = (int32_t)K;
-  p.num_m_blk = (int32_t)((M + b200::kBM - 1) / b200::kBM);
-  p.num_n_blk = (int32_t)((N + kBN - 1) / kBN);
+  p.num_m_blk = (int32_t)((M + bm - 1) / bm);
+  p.num_n_blk = (int32_t)((N + bn - 1) / bn);
   p.num_k_blk = (int32_t)((K + b200::kBK - 1) / b200::kBK);
   const int64_t tiles = (int64_t)p.num_m_blk * p.num_n_blk;
   if (tiles > kLim) return B200_ERR_TOO_LARGE;
@@ -154,10 +191,30 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
   p.timeout_ns = st->timeout_ns;
   p.status = st->status_ptr;
 
-  const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
-  auto kern = b200::gemm_bf16_tcgen05_kernel<kBN, kStages>;
-  kern<<<grid, b200::kNumThreads, b200::SmemPlan<kBN, kStages>::kAllocBytes, stream>>>(tmA, tmB, tmC, p);
-  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  if (!use_pair) {
+    const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
+    auto kern = p.b_mn_major ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>
+                             : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>;
+    kern<<<grid, b200::kNumThreads, b200::SmemPlan<kBN, kStages>::kAllocBytes, stream>>>(tmA, tmB, tmC, p);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  }
+  const int pairs = (int)(tiles < st->max_pairs ? tiles : st->max_pairs);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>, tmA, tmB, tmC, p)
+                   : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>, tmA, tmB, tmC, p);
+  return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
 extern "C" B200_API int b200_gemm_status(void* stream_, uint32_t* device_bits) {

@@ -87,7 +87,7 @@ __device__ __forceinline__ void raise_status(const GemmParams& p, volatile uint3
   if (p.status != nullptr) atomicOr(p.status, code);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool B_MN>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           mbar_arrive_expect_tx(fb, Plan::kStageBytes);
           tma_load_2d(sA + stage * Plan::kABytes, &tmA, fb, kb * kBK, mb * kBM, pol);
           const uint32_t dstB = sB + stage * Plan::kBBytes;
-          if (p.b_mn_major == 0u) {
+          if constexpr (!B_MN) {
             tma_load_2d(dstB, &tmB, fb, kb * kBK, nb * BN, pol);
           } else {
 #pragma unroll
@@ -194,7 +194,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer ---------------------------------------------------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, BN, false, p.b_mn_major != 0u);
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, false, B_MN);
+      // Stage-0 descriptors (layouts as in gemm_sm100_pair.cuh); stages and
+      // K slices only advance the start-address field.
+      const uint64_t a_desc0 = smem_desc_sw128(sA, 16, 1024);
+      const uint64_t b_desc0 = B_MN ? smem_desc_sw128(sB, 64 * kBK * 2, 1024) : smem_desc_sw128(sB, 16, 1024);
+      constexpr uint32_t kBStep = B_MN ? (2048 >> 4) : (32 >> 4);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -213,18 +218,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = sA + stage * Plan::kABytes;
-          const uint32_t b0 = sB + stage * Plan::kBBytes;
+          const uint64_t ad = a_desc0 + (uint64_t)((stage * Plan::kABytes) >> 4);
+          const uint64_t bd = b_desc0 + (uint64_t)((stage * Plan::kBBytes) >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            // K-major SW128 operand: rows of 128 bytes, 8-row groups 1024 bytes apart;
-            // the k-th 16-wide K slice starts 32 bytes into each row.
-            const uint64_t ad = smem_desc_sw128(a0 + k * 32, 16, 1024);
-            // MN-major SW128 operand (B as [K,N]): 64-wide N atoms 8 KiB apart (LBO),
-            // 8-row K groups 1024 bytes apart (SBO); the k-th K slice is 16 rows = 2 KiB on.
-            const uint64_t bd = p.b_mn_major ? smem_desc_sw128(b0 + k * 2048, 64 * kBK * 2, 1024)
-                                             : smem_desc_sw128(b0 + k * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16(d_tmem, ad + 2u * k, bd + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(empty_bar(stage));  // stage is free once these MMAs have read it
           if (++stage == STAGES) {

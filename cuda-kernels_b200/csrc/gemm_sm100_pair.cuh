@@ -1,0 +1,301 @@
+// CTA-pair (cta_group::2) variant of the persistent BF16 GEMM for sm_100a.
+//
+// Same contract as gemm_sm100.cuh (C = A x op(B), bf16 in, fp32 accumulate,
+// bf16 out, B either [N,K] or [K,N]), but each output tile of 256 x BN is
+// computed by the two CTAs of a cluster together:
+//
+//   * CTA r (r = 0, 1) TMA-loads rows [128r, 128r+128) of the A tile and
+//     columns [r*BN/2, (r+1)*BN/2) of the B tile into its own shared memory.
+//     Both CTAs' loads signal the leader's (r = 0) "full" barrier.  Each CTA
+//     therefore streams half of B instead of all of it, which halves the B
+//     traffic per SM relative to a 128 x BN single-CTA tile with the same
+//     accumulator size.  Loads are plain (one destination each).
+//   * One thread of the leader issues tcgen05.mma.cta_group::2 with M = 256:
+//     the tensor cores of both SMs read both CTAs' operand halves and each
+//     SM accumulates its own 128 rows x BN columns in its own TMEM.
+//   * The leader's tcgen05.commit (one instruction signalling both CTAs'
+//     barriers) releases ring stages and hands finished accumulators to the
+//     epilogue warps of both CTAs; each CTA's epilogue
+//     drains its own TMEM and TMA-stores its 128 rows.  The accumulator is
+//     double-buffered in TMEM so the epilogue overlaps the next tile.
+//
+// Every mbarrier wait is bounded (ptx_sm100.cuh: mbar_wait).  The only
+// unbounded waits are the two full-cluster barriers at set-up and teardown,
+// which every thread of both CTAs reaches because all other waits end.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "gemm_sm100.cuh"
+#include "ptx_sm100.cuh"
+
+namespace b200 {
+
+constexpr int kPairBM = 256;  // rows of C per pair tile (128 per CTA)
+
+template <int BN, int STAGES>
+struct PairSmemPlan {
+  static constexpr int kHalfN = BN / 2;
+  static constexpr int kABytes = kBM * kBK * 2;        // this CTA's 128 rows of A: 16 KiB
+  static constexpr int kBBytes = kHalfN * kBK * 2;     // this CTA's half of B: 16 KiB for BN = 256
+  static constexpr int kStageBytes = kABytes + kBBytes;  // per CTA
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + STAGES * kABytes;
+  static constexpr int kOffC = kOffB + STAGES * kBBytes;
+  static constexpr int kOffBar = kOffC + kEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1;
+  static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
+  static constexpr int kOffAbort = kOffTmemHolder + 4;
+  static constexpr int kBytes = kOffAbort + 4;
+  static constexpr int kAllocBytes = kBytes + 1024;
+  static_assert(kAllocBytes <= 232448, "shared memory plan exceeds 227 KiB");
+  static_assert(kHalfN % 64 == 0, "each CTA's half of the B tile must be whole 64-column swizzle atoms");
+};
+
+template <int BN, int STAGES, bool B_MN>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using Plan = PairSmemPlan<BN, STAGES>;
+  constexpr int kHalfN = Plan::kHalfN;
+  static_assert(BN % kEpiCols == 0 && BN >= 128 && BN <= 256, "BN must be 128..256 in steps of 64");
+  static_assert(kAccBufs * BN <= kTmemCols, "accumulators must fit in TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_u32);
+
+  const uint32_t sA = base + Plan::kOffA;
+  const uint32_t sB = base + Plan::kOffB;
+  const uint32_t sC = base + Plan::kOffC;
+  const uint32_t bar0 = base + Plan::kOffBar;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto accf_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + kAccBufs + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 2 * kAccBufs);
+  volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t rank = cluster_ctarank();  // 0 = MMA leader of the pair
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  // ---- set-up -------------------------------------------------------------
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);   // leader's producer arrive + both CTAs' transaction bytes
+      mbar_init(empty_bar(s), 1);  // one commit from the leader's MMA thread
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(accf_bar(b), 1);              // one commit from the leader's MMA thread
+      mbar_init(acce_bar(b), 2 * kEpiWarps);  // (leader's copy) every epilogue warp of the pair
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(const_cast<uint32_t*>(tmem_holder)), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive / transaction
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ---- TMA producer (both CTAs) ---------------------------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        const int row0 = mb * kPairBM + (int)rank * kBM;
+        const int col0 = nb * BN + (int)rank * kHalfN;
+        for (int kb = 0; kb < p.num_k_blk; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = mapa_shared(full_bar(stage), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * Plan::kStageBytes);
+          tma_load_2d_pair(sA + stage * Plan::kABytes, &tmA, fb, kb * kBK, row0, pol);
+          const uint32_t dstB = sB + stage * Plan::kBBytes;
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(dstB, &tmB, fb, kb * kBK, col0, pol);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kHalfN / 64; ++j) {
+              tma_load_2d_pair(dstB + j * (64 * kBK * 2), &tmB, fb, col0 + 64 * j, kb * kBK, pol);
+            }
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) raise_status(p, abort_flag, kDevTimeoutProducer);
+      // Drain (leader): the leader's full barriers count the bytes of both CTAs'
+      // loads, so once the most recent phase of each has completed, nothing
+      // either CTA loaded is still in flight.  The follower's own loads are
+      // covered by this wait plus the teardown cluster barrier.
+      if (rank == 0) {
+        const uint32_t nst = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+        for (uint32_t i = 0; i < nst; ++i) {
+          const uint32_t it = issued - 1u - i;
+          if (!mbar_wait(full_bar(it % STAGES), (it / STAGES) & 1u, p.timeout_ns, nullptr)) {
+            raise_status(p, abort_flag, kDevTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer (leader CTA only) ---------------------------------------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kPairBM, BN, false, B_MN);
+      // Descriptors of stage 0; later stages and K slices only move the
+      // start-address field (bits 0..13, address >> 4), which never carries.
+      //   A, K-major SW128: 128-byte rows, 8-row groups 1024 B apart; the k-th
+      //     16-wide K slice starts 32 B into each row.
+      //   B, K-major: same as A.  B, MN-major ([K,N] source): 64-column atoms
+      //     8 KiB apart (LBO), 8-row K groups 1024 B apart (SBO); the k-th K
+      //     slice starts 16 rows = 2 KiB on.
+      const uint64_t a_desc0 = smem_desc_sw128(sA, 16, 1024);
+      const uint64_t b_desc0 = B_MN ? smem_desc_sw128(sB, 64 * kBK * 2, 1024) : smem_desc_sw128(sB, 16, 1024);
+      constexpr uint32_t kBStep = B_MN ? (2048 >> 4) : (32 >> 4);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+        if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_k_blk; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = a_desc0 + (uint64_t)((stage * Plan::kABytes) >> 4);
+          const uint64_t bd = b_desc0 + (uint64_t)((stage * Plan::kBBytes) >> 4);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            umma_bf16_pair(d_tmem, ad + 2u * k, bd + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          // Stage `stage` is free in both CTAs once these MMAs have read it.
+          umma_commit_pair_both(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_both(accf_bar(acc));  // accumulator ready for both CTAs' epilogues
+        if (++acc == kAccBufs) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) raise_status(p, abort_flag, kDevTimeoutMma);
+      umma_commit_pair(mapa_shared(drain_bar, 0));
+      if (!mbar_wait(drain_bar, 0u, p.timeout_ns, nullptr)) raise_status(p, abort_flag, kDevTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue (warps 2..5 of both CTAs) ------------------------------------------
+    const int q = warp & 3;
+    const int slot = warp - 2;
+    const uint32_t tmem_lane = (uint32_t)(q * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sbuf = 0;
+    for (int t = pair; t < p.num_tiles; t += num_pairs) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const bool got = mbar_wait(accf_bar(acc), acc_phase, p.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) raise_status(p, abort_flag, kDevTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + tmem_lane + (uint32_t)(acc * BN);
+      const int row = mb * kPairBM + (int)rank * kBM + q * kEpiRowsPerWarp;
+#pragma unroll 1
+      for (int c = 0; c < BN / kEpiCols; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_row + c * kEpiCols, r0);
+        tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, r1);
+        tmem_ld_wait_regs(r0);
+        tmem_ld_wait_regs(r1);
+        if (c == BN / kEpiCols - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(acce_bar(acc), 0));
+        }
+        const uint32_t buf = sC + (uint32_t)((slot * 2 + sbuf) * kEpiBufBytes);
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = buf + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* src = (j < 4) ? &r0[j * 8] : &r1[(j - 4) * 8];
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(src[2 * e]), __uint_as_float(src[2 * e + 1]));
+            w[e] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                       "r"(w[3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, nb * BN + c * kEpiCols, row);
+          bulk_commit_group();
+        }
+        sbuf ^= 1;
+      }
+      if (++acc == kAccBufs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ---- teardown -------------------------------------------------------------
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its barriers or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b200

@@ -1,8 +1,8 @@
 // Hand-written PTX wrappers for the sm_100a BF16 GEMM.
 //
 // Everything the kernel needs from Blackwell is here, written directly against
-// the PTX ISA: mbarriers with bounded waits, TMA tensor loads/stores (never with
-// cluster multicast), and the tcgen05 family (TMEM alloc/dealloc, UMMA issue,
+// the PTX ISA: mbarriers with bounded waits, plain TMA tensor loads/stores
+// (each load has exactly one destination CTA), and the tcgen05 family (TMEM alloc/dealloc, UMMA issue,
 // commit, TMEM->register loads, ordering fences).
 //
 // The reference's own helpers (bf16_matmul/common.hpp:35-167) cover the sm_80/
@@ -105,7 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor) — plain, never .multicast::cluster
+// TMA (cp.async.bulk.tensor) — plain loads only: one source, one destination CTA
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -230,6 +230,93 @@ __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
         "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
       :
       : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters and the 2-CTA ("CTA pair") forms of tcgen05 / TMA.
+// A pair = the two CTAs of a cluster of size 2; rank 0 is the MMA leader.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address, in the shared::cluster window, of the object at the same offset
+// as `local_addr` in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+// Full cluster barrier (every thread of every CTA of the cluster).  Used once
+// after set-up and once before teardown; all other waits are bounded, so every
+// CTA reaches it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier that may live in another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is signalled
+// on `bar_cluster`, an mbarrier of either CTA of the pair (the leader's).
+// A plain load: one source, one destination CTA.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster, int32_t x,
+                                                 int32_t y, uint64_t l2_policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_cluster), "l"(l2_policy)
+      : "memory");
+}
+
+// TMEM allocation shared by the pair: one warp in each of the two CTAs executes it.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair UMMA, issued by one thread of the leader CTA: D (each CTA's TMEM holds
+// its own 128 rows) (+)= A (each CTA's smem holds its 128 rows) x B^T (each
+// CTA's smem holds half of the N columns).  Descriptors name CTA-local offsets,
+// which are identical in both CTAs.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Completion signal (not a copy): when every tcgen05 operation issued so far
+// by this thread has completed, arrive once on the mbarrier at CTA-local
+// offset `bar` in each CTA of the pair (cta_mask 0b11).  One instruction
+// signals both CTAs; issuing a separate commit per CTA costs tensor-pipe time
+// on every ring stage.
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+// Completion signal to one mbarrier at shared::cluster address `bar_cluster`.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -70,3 +70,18 @@ def test_product_path_does_not_touch_oracle():
             if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
                 txt = open(os.path.join(root, f), errors="ignore").read()
                 assert "oracle" not in re.sub(r"#.*|//.*", "", txt).lower() or f == "build.py", f
+
+
+def test_torch_binding_rejects_bad_arguments_on_cpu():
+    """The reference-shaped torch binding raises (never crashes) on bad input;
+    these checks run before any CUDA call, so they need no GPU."""
+    import torch
+    from b200_gemm.binding import load_binding
+    ext = load_binding()
+    a = torch.zeros((64, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ext.matmul_b200(a, a)
+    with pytest.raises(ValueError, match="bfloat16"):
+        ext.matmul_b200(a.float(), a)
+    with pytest.raises(ValueError, match="bfloat16"):
+        ext.matmul_b200_kn(a, a.half())

@@ -153,10 +153,12 @@ def test_torch_binding_matches_c_abi():
     torch.cuda.synchronize()
     assert c1.shape == (300, 200)  # N from B.size(0), unlike the reference's B.size(1)
     assert torch.equal(c1, c2) and torch.equal(c1, c3)
-    with pytest.raises(RuntimeError):
+    with pytest.raises(ValueError, match="bfloat16"):
         ext.matmul_b200(a.float(), b)
-    with pytest.raises(RuntimeError):
+    with pytest.raises(ValueError, match="inner dimensions differ"):
         ext.matmul_b200(a, b[:, :100])
+    with pytest.raises(ValueError, match="CUDA"):
+        ext.matmul_b200(a.cpu(), b.cpu())
 
 
 def test_k_zero_m_zero_and_streams():
