@@ -84,4 +84,4 @@ def test_torch_binding_rejects_bad_arguments_on_cpu():
     with pytest.raises(ValueError, match="bfloat16"):
         ext.matmul_b200(a.float(), a)
     with pytest.raises(ValueError, match="bfloat16"):
-        ext.matmul_b200_kn(a, a.half())
+        ext.matmul_b200_kn(a.half(), a)
