@@ -210,6 +210,175 @@ def run_reference(args, world, rank):
     return 0
 
 
+def sweep_configs():
+    """Single-GPU BASELINE configs 1-4 (config 5 is the multi-GPU row-sharded job)."""
+    out = []
+    for n in (1024, 2048, 4096, 8192, 16384):
+        out.append(("square", n, n, n, "uniform"))
+    for m in (16, 64, 128):
+        for (n, k) in ((4096, 4096), (14336, 4096), (4096, 14336)):
+            out.append(("skinny", m, n, k, "normal"))
+    for m in (8192, 8191, 5000):
+        for (n, k) in ((4096, 4096), (6144, 4096), (28672, 4096), (4096, 14336), (128256, 4096)):
+            out.append(("projection", m, n, k, "normal"))
+    return out
+
+
+def time_config(M, N, K, layout, dist_kind, b200_gemm, target_ms=250.0, warmup=10, with_cublas=True, use_graph=True):
+    """Device-time one GEMM shape back to back over rotating buffer sets larger than L2."""
+    import math
+    import torch
+    dev = torch.device("cuda", torch.cuda.current_device())
+    set_bytes = 2 * (M * K + K * N + M * N)
+    R = max(2, math.ceil(400e6 / set_bytes))
+    g = torch.Generator(device=dev).manual_seed(M * 31 + N * 7 + K)
+
+    def gen(shape, std=1.0):
+        if dist_kind == "uniform":
+            return (torch.rand(shape, generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+        return (torch.randn(shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+    b_shape = (K, N) if layout == "kn" else (N, K)
+    A = [gen((M, K)) for _ in range(R)]
+    B = [gen(b_shape, 1.0 if dist_kind == "uniform" else K ** -0.5) for _ in range(R)]
+    C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(R)]
+
+    def ours(i):
+        b200_gemm.gemm(A[i % R], B[i % R], b_layout=layout, out=C[i % R])
+
+    def cublas(i):
+        torch.matmul(A[i % R], B[i % R] if layout == "kn" else B[i % R].t(), out=C[i % R])
+
+    res = {}
+    for name, fn in (("b200", ours), ("cublas", cublas)):
+        if name == "cublas" and not with_cublas:
+            continue
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(3):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        est = max(e0.elapsed_time(e1) / 3, 1e-3)
+        if use_graph and est < 1.0:
+            # Short GEMMs: replay a captured batch so that host launch cost is
+            # not timed (both implementations are measured the same way).
+            per = R * max(1, int(2.0 / (est * R)))
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                fn(0)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(graph, stream=s):
+                    for i in range(per):
+                        fn(i)
+            torch.cuda.synchronize()
+            graph.replay()
+            torch.cuda.synchronize()
+            reps = max(3, int(target_ms / (est * per)))
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = e0.elapsed_time(e1) / (reps * per)
+            del graph
+            continue
+        steps = max(5, int(target_ms / est))
+        e0.record()
+        for i in range(steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / steps
+    b200_gemm.check_status()
+    del A, B, C
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_sweep(args) -> int:
+    """--sweep: one JSON line per single-GPU BASELINE config (b200 and cuBLAS, same loop)."""
+    import torch
+    torch.cuda.set_device(0)
+    import b200_gemm
+    peaks = _peaks()
+    for family, M, N, K, dist_kind in sweep_configs():
+        for layout in (("kn", "nk") if (family == "square" and M == 4096) or family == "skinny" else ("kn",)):
+            t = time_config(M, N, K, layout, dist_kind, b200_gemm, with_cublas=not args.no_cublas,
+                            use_graph=not args.no_graph)
+            flops = 2.0 * M * N * K
+            nbytes = 2.0 * (M * K + K * N + M * N)
+            tf = flops / (t["b200"] / 1e3) / 1e12
+            gbs = nbytes / (t["b200"] / 1e3) / 1e9
+            hbm_bound = nbytes / (peaks["hbm_gbs"] * 1e9) > flops / (peaks["burst"] * 1e12)
+            line = {"config": {"family": family, "M": M, "N": N, "K": K, "b_layout": layout, "data": dist_kind},
+                    "ms": round(t["b200"], 5), "tflops": round(tf, 1), "gbs": round(gbs, 1),
+                    "bound": "hbm" if hbm_bound else "tensor",
+                    "frac": round(gbs / peaks["hbm_gbs"] if hbm_bound else tf / peaks["burst"], 4),
+                    "peak_source": peaks["source"], "timing": "graph replay" if (not args.no_graph and t["b200"] < 1.0) else "direct launches"}
+            if "cublas" in t:
+                line["cublas_ms"] = round(t["cublas"], 5)
+                line["speedup_vs_cublas"] = round(t["cublas"] / t["b200"], 3)
+            print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_rowshard(args) -> int:
+    """--rowshard: BASELINE config 5, M=131072, N=K=8192 split into row panels
+    over the ranks (strong scaling).  Each step: B broadcast from rank 0 over
+    NCCL (in N-chunks overlapped with the GEMM, B stored [N,K]) + the GEMM of
+    every panel; device time, max over ranks.  Also reports the GEMM alone."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = _dist_setup()
+    import b200_gemm
+    from b200_gemm.dist import row_sharded_gemm, shard_rows
+    M, N, K = args.rowshard_m, 8192, 8192
+    dev = torch.device("cuda", torch.cuda.current_device())
+    s, e = shard_rows(M, world, rank)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    a = (torch.rand((e - s, K), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    b = (torch.rand((N, K), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    c = torch.empty((e - s, N), dtype=torch.bfloat16, device=dev)
+
+    def step(bcast):
+        row_sharded_gemm(a, b, M=M, b_layout="nk", chunks=args.chunks, out=c, broadcast=bcast)
+
+    res = {}
+    for name, bcast in (("gemm_only", False), ("broadcast_plus_gemm", world > 1)):
+        for _ in range(max(args.warmup, 3)):
+            step(bcast)
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step(bcast)
+        e1.record()
+        torch.cuda.synchronize()
+        _barrier(world)
+        res[name] = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    b200_gemm.check_status()
+    flops = 2.0 * M * N * K
+    if rank == 0:
+        print(json.dumps({
+            "metric": "bf16_gemm_tflops_rowshard_131072x8192x8192", "n_gpus": world, "steps": args.steps,
+            "value": round(flops / (res["broadcast_plus_gemm"] / 1e3) / 1e12, 2), "unit": "TFLOPS",
+            "ms_per_step": round(res["broadcast_plus_gemm"], 4), "gemm_only_ms": round(res["gemm_only"], 4),
+            "gemm_only_tflops": round(flops / (res["gemm_only"] / 1e3) / 1e12, 2), "scaling": "strong",
+            "config": {"M": M, "N": N, "K": K, "b_layout": "nk", "chunks": args.chunks,
+                       "panel_rows": e - s, "timing": "device, max over ranks"}}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -222,7 +391,17 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-rows", type=int, default=256)
+    ap.add_argument("--sweep", action="store_true", help="time every single-GPU BASELINE config (one line each)")
+    ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="sweep: time direct launches instead of graph replay")
+    ap.add_argument("--rowshard", action="store_true", help="BASELINE config 5: row-sharded 131072x8192x8192")
+    ap.add_argument("--rowshard-m", type=int, default=131072)
+    ap.add_argument("--chunks", type=int, default=4)
     args = ap.parse_args(argv)
+    if args.rowshard:
+        return run_rowshard(args)
+    if args.sweep:
+        return run_sweep(args)
     if args.warmup < 3:
         args.warmup = 3
     args.e2e_steps = max(args.e2e_steps, 1)

@@ -23,6 +23,11 @@ B200_ERR_TOO_LARGE = 7
 B200_B_NK = 0
 B200_B_KN = 1
 
+B200_KERNEL_AUTO = 0
+B200_KERNEL_SINGLE = 1
+B200_KERNEL_PAIR = 2
+B200_KERNEL_SKINNY = 3
+
 # Every symbol include/b200_gemm.h declares, with its ctypes signature.
 _SIGNATURES = {
     "b200_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
@@ -31,6 +36,8 @@ _SIGNATURES = {
                                       ctypes.c_int, ctypes.c_void_p]),
     "b200_gemm_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "b200_gemm_set_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
+    "b200_gemm_set_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "b200_gemm_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "b200_gemm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "b200_gemm_version": (ctypes.c_char_p, []),
 }

@@ -1,0 +1,150 @@
+"""Single-node multi-GPU driver for the row-sharded BF16 GEMM.
+
+The job (BASELINE config "row-sharded large GEMM"): C = A @ B with A split
+into contiguous row panels, one per rank (one process per GPU); B is
+broadcast once from a source rank with NCCL over NVLink; each rank multiplies
+its panel with the local copy of B on its own GPU; C stays sharded, and an
+optional all-gather assembles it.
+
+The reference has no multi-GPU code at all (typr7/CUDA-Kernels is a
+single-GPU kernel collection); this driver is new.  Design points:
+
+  * B is broadcast in column chunks when it is stored [N,K] (each chunk is a
+    contiguous block of B's rows), on a side stream; the GEMM of chunk j runs
+    on the compute stream as soon as chunk j has arrived (CUDA event), so
+    the broadcast overlaps the GEMM of the chunks before it.  [K,N] B is
+    broadcast whole (its column chunks are not contiguous).
+  * No kernel reads another GPU's memory: B lands in each GPU's own HBM
+    first.
+  * The GEMM is pluggable (`gemm_fn`) so the host logic can be tested with
+    CPU ranks (gloo) and a CPU GEMM; the default is b200_gemm.gemm.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) of rank's contiguous row panel; the first M % world ranks get one extra row."""
+    if world <= 0 or not (0 <= rank < world) or M < 0:
+        raise ValueError(f"bad shard request M={M} world={world} rank={rank}")
+    base, extra = divmod(M, world)
+    start = rank * base + min(rank, extra)
+    stop = start + base + (1 if rank < extra else 0)
+    return start, stop
+
+
+def chunk_bounds(N: int, chunks: int, align: int = 64) -> list[tuple[int, int]]:
+    """Split [0, N) into at most `chunks` pieces whose starts are multiples of `align`
+    (keeps every output column offset 16-byte aligned for TMA)."""
+    if N <= 0:
+        return []
+    chunks = max(1, min(chunks, (N + align - 1) // align))
+    step = ((N + chunks - 1) // chunks + align - 1) // align * align
+    out = []
+    s = 0
+    while s < N:
+        out.append((s, min(s + step, N)))
+        s += step
+    return out
+
+
+GemmFn = Callable[..., torch.Tensor]
+
+
+def _default_gemm(a, b, *, b_layout, out):
+    import b200_gemm
+    return b200_gemm.gemm(a, b, b_layout=b_layout, out=out)
+
+
+@dataclass
+class ShardedResult:
+    c_local: torch.Tensor  # this rank's row panel of C
+    row_start: int
+    row_stop: int
+
+
+def broadcast_b(b: torch.Tensor, src: int = 0, group=None) -> None:
+    """Broadcast B from `src` to every rank of `group` in place."""
+    dist.broadcast(b, src=src, group=group)
+
+
+def row_sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, *, M: int, b_layout: str = "kn", src: int = 0,
+                     group=None, chunks: int = 4, out: torch.Tensor | None = None,
+                     gemm_fn: GemmFn | None = None, broadcast: bool = True) -> ShardedResult:
+    """One row-sharded GEMM step on this rank.
+
+    a_local : this rank's panel A[start:stop, :] (shape [stop-start, K])
+    b       : on `src`, the full B; on the other ranks, a buffer of the same
+              shape and dtype that receives it (unless broadcast=False, in
+              which case every rank already holds B)
+    M       : global number of rows of A (used to check the panel size)
+    """
+    gemm_fn = gemm_fn or _default_gemm
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    start, stop = shard_rows(M, world, rank)
+    if a_local.shape[0] != stop - start:
+        raise ValueError(f"rank {rank}: A panel has {a_local.shape[0]} rows, expected {stop - start}")
+    K = a_local.shape[1]
+    N = b.shape[0] if b_layout == "nk" else b.shape[1]
+    if (b.shape[1] if b_layout == "nk" else b.shape[0]) != K:
+        raise ValueError("inner dimensions of the A panel and B differ")
+    if out is None:
+        out = torch.empty((stop - start, N), dtype=a_local.dtype, device=a_local.device)
+
+    use_streams = a_local.is_cuda
+    if not broadcast or world == 1:
+        gemm_fn(a_local, b, b_layout=b_layout, out=out)
+        return ShardedResult(out, start, stop)
+
+    if b_layout != "nk" or chunks <= 1:
+        broadcast_b(b, src, group)
+        gemm_fn(a_local, b, b_layout=b_layout, out=out)
+        return ShardedResult(out, start, stop)
+
+    # [N,K] B: broadcast row blocks of B on a side stream, multiply each block
+    # as soon as it has arrived.
+    bounds = chunk_bounds(N, chunks)
+    if use_streams:
+        compute = torch.cuda.current_stream(a_local.device)
+        comm = torch.cuda.Stream(device=a_local.device)
+        comm.wait_stream(compute)
+        events = []
+        with torch.cuda.stream(comm):
+            for (s, e) in bounds:
+                dist.broadcast(b[s:e], src=src, group=group)
+                ev = torch.cuda.Event()
+                ev.record(comm)
+                events.append(ev)
+        for (s, e), ev in zip(bounds, events):
+            compute.wait_event(ev)
+            gemm_fn(a_local, b[s:e], b_layout="nk", out=out[:, s:e])
+        b.record_stream(comm)
+    else:
+        for (s, e) in bounds:
+            dist.broadcast(b[s:e], src=src, group=group)
+            gemm_fn(a_local, b[s:e], b_layout="nk", out=out[:, s:e])
+    return ShardedResult(out, start, stop)
+
+
+def gather_rows(c_local: torch.Tensor, M: int, group=None) -> torch.Tensor:
+    """All-gather the row panels of C into the full [M, N] matrix on every rank."""
+    world = dist.get_world_size(group)
+    sizes = [shard_rows(M, world, r) for r in range(world)]
+    N = c_local.shape[1]
+    if all((e - s) == (sizes[0][1] - sizes[0][0]) for s, e in sizes):
+        full = torch.empty((M, N), dtype=c_local.dtype, device=c_local.device)
+        dist.all_gather_into_tensor(full, c_local.contiguous(), group=group)
+        return full
+    # Ragged panels: gather padded panels, then drop the padding rows.
+    rows = sizes[0][1] - sizes[0][0]
+    padded = torch.zeros((rows, N), dtype=c_local.dtype, device=c_local.device)
+    padded[: c_local.shape[0]] = c_local
+    stacked = torch.empty((world * rows, N), dtype=c_local.dtype, device=c_local.device)
+    dist.all_gather_into_tensor(stacked, padded, group=group)
+    return torch.cat([stacked[r * rows: r * rows + (e - s)] for r, (s, e) in enumerate(sizes)], dim=0)

@@ -101,3 +101,16 @@ def set_timeout_ns(ns: int, device: torch.device | int | None = None) -> None:
         rc = lib.b200_gemm_set_timeout_ns(int(ns))
     if rc != _lib.B200_OK:
         raise B200GemmError(rc)
+
+
+_KERNELS = {"auto": _lib.B200_KERNEL_AUTO, "single": _lib.B200_KERNEL_SINGLE, "pair": _lib.B200_KERNEL_PAIR,
+            "skinny": _lib.B200_KERNEL_SKINNY}
+
+
+def set_kernel(which: str) -> None:
+    """Force a kernel for later calls ("auto", "single", "pair", "skinny"); for tests and tuning."""
+    if which not in _KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
+    rc = _lib.load().b200_gemm_set_kernel(_KERNELS[which])
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc)

@@ -7,11 +7,12 @@
 //     void(const nv_bfloat16* A, const nv_bfloat16* B, nv_bfloat16* C, int M, int N, int K)
 // (bf16_matmul/profile_entry.cpp:9-14, bf16_matmul/matmul.cpp:5-10).
 //
-// This file is self-contained: it compiles the library sources into the same
-// translation unit, so `CUDA_ARCH=sm_100a scripts/profile.sh bf16_matmul/matmul_b200.cu`
-// (with this file placed beside the reference's profile_entry.cpp) links with no
-// extra flags — the tensor-map encoder is fetched through the runtime, so no
-// -lcuda is needed either.
+// This file compiles the library sources into the same translation unit, so
+// with this file placed beside the reference's profile_entry.cpp,
+//   CUDA_ARCH=sm_100a EXTRA_NVCC_FLAGS="-I<repo>/include -I<repo>/cuda-kernels_b200/csrc" \
+//     scripts/profile.sh bf16_matmul/matmul_b200.cu
+// builds and links it; the tensor-map encoder is fetched through the runtime,
+// so no -lcuda is needed.
 //
 // Semantics match the reference launchers: A [M,K] row-major, B [N,K] row-major
 // (C = A * B^T), C [M,N] row-major, legacy default stream, asynchronous.  Where
@@ -21,7 +22,7 @@
 
 #include <cuda_bf16.h>
 
-#include "../csrc/b200_gemm.cu"
+#include "b200_gemm.cu"  // cuda-kernels_b200/csrc/ (pass -I to it and to include/)
 
 void matmul_b200(const nv_bfloat16* A, const nv_bfloat16* B, nv_bfloat16* C, int M, int N, int K) {
   const int rc = b200_gemm_bf16(A, B, C, M, N, K, K, K, N, B200_B_NK, nullptr);

@@ -10,13 +10,15 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
 
-#include "../../include/b200_gemm.h"
+#include "b200_gemm.h"  // include/ (pass -I <repo>/include)
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
+#include "gemm_sm100_skinny.cuh"
 
 namespace {
 
@@ -35,6 +37,23 @@ constexpr int kStages = 4;
 constexpr int kPairBN = 256;
 constexpr int kPairStages = 6;
 constexpr int kGroupM = 16;
+
+// Skinny (M <= 128) configurations: UMMA N = MPAD, ring depth per MPAD.
+template <int MPAD>
+struct SkinnyCfg;
+template <>
+struct SkinnyCfg<16> { static constexpr int kStages = 10; };
+template <>
+struct SkinnyCfg<32> { static constexpr int kStages = 9; };
+template <>
+struct SkinnyCfg<64> { static constexpr int kStages = 8; };
+template <>
+struct SkinnyCfg<128> { static constexpr int kStages = 6; };
+constexpr int kMaxClusterSplits = 8;  // portable cluster size limit
+
+// Kernel selection override (b200_gemm_set_kernel): process-wide.
+enum ForceKernel { kForceAuto = 0, kForceSingle = 1, kForcePair = 2, kForceSkinny = 3 };
+std::atomic<int> g_force_kernel{kForceAuto};
 
 struct DeviceState {
   std::once_flag once;
@@ -60,6 +79,18 @@ void load_encode_fn() {
   }
 }
 
+template <int MPAD>
+int set_skinny_attrs() {
+  constexpr int st = SkinnyCfg<MPAD>::kStages;
+  constexpr int smem = b200::SkinnySmemPlan<MPAD, st>::kAllocBytes;
+  if (cudaFuncSetAttribute(b200::gemm_bf16_skinny_kernel<MPAD, st, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess ||
+      cudaFuncSetAttribute(b200::gemm_bf16_skinny_kernel<MPAD, st, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return B200_ERR_CUDA;
+  return B200_OK;
+}
+
 int init_device(int dev, DeviceState& st) {
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return B200_ERR_CUDA;
@@ -78,6 +109,9 @@ int init_device(int dev, DeviceState& st) {
                            cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess ||
       cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (set_skinny_attrs<16>() != B200_OK || set_skinny_attrs<32>() != B200_OK || set_skinny_attrs<64>() != B200_OK ||
+      set_skinny_attrs<128>() != B200_OK)
     return B200_ERR_CUDA;
   auto pkern = b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>;
   {
@@ -112,22 +146,124 @@ int current_device_state(DeviceState** out) {
   return B200_OK;
 }
 
-// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
-// `pitch_elems` elements between rows, box {box_inner, box_outer}, 128B swizzle.
-int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
-              uint32_t box_inner, uint32_t box_outer, bool is_load) {
+// Tensor maps are pure host-side descriptors; repeated calls on the same
+// buffers (the common case for weights and reused activations) skip the
+// encode.  One small cache per host thread: no locking on the launch path.
+struct TmapKey {
+  const void* ptr;
+  uint64_t inner, outer, pitch;
+  uint32_t box_inner, box_outer;
+  uint32_t flags;
+  bool operator==(const TmapKey& o) const {
+    return ptr == o.ptr && inner == o.inner && outer == o.outer && pitch == o.pitch && box_inner == o.box_inner &&
+           box_outer == o.box_outer && flags == o.flags;
+  }
+};
+constexpr int kTmapCacheSize = 32;
+struct TmapCache {
+  TmapKey key[kTmapCacheSize];
+  CUtensorMap map[kTmapCacheSize];
+  bool used[kTmapCacheSize] = {};
+  int next = 0;
+};
+thread_local TmapCache t_tmap_cache;
+
+int encode_2d_uncached(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
+                       uint32_t box_inner, uint32_t box_outer, bool is_load, bool swizzle) {
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {pitch_elems * 2};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         is_load ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
+// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
+// `pitch_elems` elements between rows, box {box_inner, box_outer}, 128B
+// swizzle unless `swizzle` is false.
+int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
+              uint32_t box_inner, uint32_t box_outer, bool is_load, bool swizzle = true) {
+  TmapCache& c = t_tmap_cache;
+  const TmapKey k{ptr, inner, outer, pitch_elems, box_inner, box_outer, (is_load ? 1u : 0u) | (swizzle ? 2u : 0u)};
+  for (int i = 0; i < kTmapCacheSize; ++i) {
+    if (c.used[i] && c.key[i] == k) {
+      *map = c.map[i];
+      return B200_OK;
+    }
+  }
+  const int rc = encode_2d_uncached(map, ptr, inner, outer, pitch_elems, box_inner, box_outer, is_load, swizzle);
+  if (rc == B200_OK) {
+    const int i = c.next;
+    c.next = (c.next + 1) % kTmapCacheSize;
+    c.key[i] = k;
+    c.map[i] = *map;
+    c.used[i] = true;
+  }
+  return rc;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Swap-AB split-K launch for M <= 128 (see gemm_sm100_skinny.cuh).
+template <int MPAD>
+int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc, int b_layout, cudaStream_t stream) {
+  constexpr int stages = SkinnyCfg<MPAD>::kStages;
+  using Plan = b200::SkinnySmemPlan<MPAD, stages>;
+  CUtensorMap tmB, tmA, tmC;
+  int rc;
+  if (b_layout == B200_B_NK) {
+    rc = encode_2d(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, b200::kBK, b200::kSkinnyBN, true);
+  } else {
+    rc = encode_2d(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, b200::kBK, true);
+  }
+  if (rc != B200_OK) return rc;
+  if ((rc = encode_2d(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, b200::kBK, MPAD, true)) != B200_OK) return rc;
+  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 32, MPAD, false, false)) != B200_OK)
+    return rc;
+
+  b200::SkinnyParams p{};
+  p.M = (int32_t)M;
+  p.N = (int32_t)N;
+  p.K = (int32_t)K;
+  p.num_k_blk = (int32_t)((K + b200::kBK - 1) / b200::kBK);
+  const int64_t n_tiles = (N + b200::kSkinnyBN - 1) / b200::kSkinnyBN;
+  if (n_tiles > 65535) return B200_ERR_TOO_LARGE;  // grid.y limit
+  // Split K so that (tiles x splits) CTAs cover the SMs once, within the
+  // cluster-size and shared-memory limits; no split is left without K-blocks.
+  int64_t splits = st.sm_count / n_tiles;
+  if (splits > kMaxClusterSplits) splits = kMaxClusterSplits;
+  if (splits > Plan::max_splits()) splits = Plan::max_splits();
+  if (splits > p.num_k_blk) splits = p.num_k_blk;
+  if (splits < 1) splits = 1;
+  p.kb_per_split = (int32_t)((p.num_k_blk + splits - 1) / splits);
+  splits = (p.num_k_blk + p.kb_per_split - 1) / p.kb_per_split;
+  p.splits = (int32_t)splits;
+  p.timeout_ns = st.timeout_ns;
+  p.status = st.status_ptr;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3((unsigned)splits, (unsigned)n_tiles, 1);
+  cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = Plan::kAllocBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      b_layout == B200_B_KN
+          ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, true>, tmB, tmA, tmC, p)
+          : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, false>, tmB, tmA, tmC, p);
+  return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
 
 }  // namespace
 
@@ -156,9 +292,18 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
   if (ldb < (b_layout == B200_B_NK ? K : N)) return B200_ERR_INVALID_ARG;
   if (!aligned16(A) || !aligned16(B) || (lda % 8) != 0 || (ldb % 8) != 0) return B200_ERR_ALIGNMENT;
 
-  // M <= 128 fits one 128-row tile per column block: the single-CTA kernel.
-  // Larger M uses CTA pairs (256-row tiles).
-  const bool use_pair = M > b200::kBM;
+  // M <= 128: swap-AB split-K kernel (HBM-bound shapes).  Larger M: CTA pairs
+  // on 256-row tiles.  (The single-CTA 128-row kernel remains for callers
+  // that force it with b200_gemm_set_kernel.)
+  const int force = g_force_kernel.load(std::memory_order_relaxed);
+  if (force == kForceSkinny && M > 128) return B200_ERR_INVALID_ARG;
+  if (force == kForceSkinny || (force == kForceAuto && M <= 128)) {
+    if (M <= 16) return launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
+    if (M <= 32) return launch_skinny<32>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
+    if (M <= 64) return launch_skinny<64>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
+    return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
+  }
+  const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM);
   const uint32_t bn = use_pair ? (uint32_t)kPairBN : (uint32_t)kBN;
   const uint32_t b_rows = use_pair ? bn / 2 : bn;  // B rows (K-major) one CTA loads per K-block
 
@@ -238,6 +383,46 @@ extern "C" B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns) {
   int rc = current_device_state(&st);
   if (rc != B200_OK) return rc;
   st->timeout_ns = timeout_ns == 0 ? kDefaultTimeoutNs : timeout_ns;
+  return B200_OK;
+}
+
+namespace {
+// One CTA waits, with the library's bounded wait, on an mbarrier that nothing
+// ever arrives at.  The wait must give up after `timeout_ns` and report it in
+// the status word — the same path a GEMM kernel takes when a role stalls.
+__global__ void selftest_wait_timeout_kernel(uint64_t timeout_ns, uint32_t* status) {
+#if B200_NO_SM100A_FEATURES
+  if (threadIdx.x == 0 && status != nullptr) atomicOr(status, (uint32_t)b200::kDevWrongArch);
+#else
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_flag;
+  if (threadIdx.x == 0) {
+    b200::mbar_init(b200::smem_u32(&bar), 1);
+    abort_flag = 0u;
+    b200::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!b200::mbar_wait(b200::smem_u32(&bar), 0u, timeout_ns, &abort_flag)) {
+      atomicOr(status, (uint32_t)b200::kDevTimeoutMma);
+    }
+  }
+#endif
+}
+}  // namespace
+
+extern "C" B200_API int b200_gemm_selftest_wait_timeout(uint64_t timeout_ns, void* stream_) {
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  if (timeout_ns == 0 || timeout_ns > 10000000000ull) return B200_ERR_INVALID_ARG;
+  selftest_wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(timeout_ns, st->status_ptr);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+extern "C" B200_API int b200_gemm_set_kernel(int which) {
+  if (which < kForceAuto || which > kForceSkinny) return B200_ERR_INVALID_ARG;
+  g_force_kernel.store(which, std::memory_order_relaxed);
   return B200_OK;
 }
 

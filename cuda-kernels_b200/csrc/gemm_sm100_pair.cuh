@@ -58,6 +58,9 @@ template <int BN, int STAGES, bool B_MN>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+#if B200_NO_SM100A_FEATURES
+  if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
+#else
   using Plan = PairSmemPlan<BN, STAGES>;
   constexpr int kHalfN = Plan::kHalfN;
   static_assert(BN % kEpiCols == 0 && BN >= 128 && BN <= 256, "BN must be 128..256 in steps of 64");
@@ -296,6 +299,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+#endif  // B200_NO_SM100A_FEATURES
 }
 
 }  // namespace b200

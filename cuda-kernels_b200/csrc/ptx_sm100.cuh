@@ -25,7 +25,19 @@ enum DeviceStatus : uint32_t {
   kDevTimeoutMma = 2u,        // MMA issuer gave up waiting for data / TMEM
   kDevTimeoutEpilogue = 4u,   // epilogue gave up waiting for an accumulator
   kDevTimeoutDrain = 8u,      // teardown gave up waiting for in-flight copies
+  kDevWrongArch = 16u,        // a copy of the kernel built without sm_100a features ran
 };
+
+// Kernel bodies use tcgen05/TMA, which exist only in the sm_100a feature set.
+// `nvcc -arch=sm_100a` (what the reference's scripts/profile.sh passes) also
+// embeds portable compute_100 PTX; in that copy the kernels compile to a stub
+// that reports kDevWrongArch.  On a B200 the sm_100a binary is always the one
+// that runs, and the host refuses devices other than compute capability 10.0.
+#if defined(__CUDA_ARCH__) && !defined(__CUDA_ARCH_FEAT_SM100_ALL)
+#define B200_NO_SM100A_FEATURES 1
+#else
+#define B200_NO_SM100A_FEATURES 0
+#endif
 
 // ---------------------------------------------------------------------------
 // Small helpers

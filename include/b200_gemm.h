@@ -89,6 +89,33 @@ B200_API int b200_gemm_status(void* stream, uint32_t* device_bits);
  */
 B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns);
 
+/*
+ * Kernel selection for later calls in this process (all devices):
+ *   B200_KERNEL_AUTO   (0) default: M <= 128 -> swap-AB split-K kernel,
+ *                          otherwise the CTA-pair kernel (256-row tiles)
+ *   B200_KERNEL_SINGLE (1) one CTA per 128 x 256 tile, any M
+ *   B200_KERNEL_PAIR   (2) CTA pair per 256 x 256 tile, any M
+ *   B200_KERNEL_SKINNY (3) swap-AB split-K, M <= 128 only (else B200_ERR_INVALID_ARG at launch)
+ * For testing and tuning; every choice computes the same product.  No
+ * reference counterpart (the reference picks a kernel by calling a different
+ * launcher, bf16_matmul/matmul.cpp:44-56).
+ */
+#define B200_KERNEL_AUTO 0
+#define B200_KERNEL_SINGLE 1
+#define B200_KERNEL_PAIR 2
+#define B200_KERNEL_SKINNY 3
+B200_API int b200_gemm_set_kernel(int which);
+
+/*
+ * Failure-detection self-test: launches one CTA that waits, with the same
+ * bounded wait every GEMM kernel uses, on an mbarrier that nothing arrives at
+ * (timeout_ns in (0, 1e10]).  The wait gives up after timeout_ns; the next
+ * b200_gemm_status() then returns B200_ERR_DEVICE_TIMEOUT, and the device
+ * stays usable.  No reference counterpart (the reference's waits spin
+ * forever, bf16_matmul/common.hpp:128-145).
+ */
+B200_API int b200_gemm_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
 /* Static text for a return code. */
 B200_API const char* b200_gemm_strerror(int code);
 

@@ -1,0 +1,63 @@
+"""Multi-GPU test of the row-sharded driver over NCCL with the B200 kernel
+(b200_gemm/dist.py).  Needs >= 2 GPUs; each rank is its own process on its
+own GPU.  B is broadcast from rank 0 in chunks overlapped with the GEMM."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, M, N, K, layout, chunks, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+    import torch.distributed as dist
+    import b200_gemm
+    from b200_gemm.dist import gather_rows, row_sharded_gemm, shard_rows
+    from tests._util import uniform_bf16
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        a_full = uniform_bf16((M, K), 11)
+        b_full = uniform_bf16((N, K) if layout == "nk" else (K, N), 12)
+        s, e = shard_rows(M, world, rank)
+        a = a_full[s:e].cuda()
+        b = b_full.cuda() if rank == 0 else torch.zeros(b_full.shape, dtype=torch.bfloat16, device="cuda")
+        res = row_sharded_gemm(a, b, M=M, b_layout=layout, chunks=chunks)
+        full = gather_rows(res.c_local, M)
+        torch.cuda.synchronize()
+        assert b200_gemm.check_status() == 0
+        assert torch.equal(b.cpu(), b_full)
+        if rank == 0:
+            torch.save(full.cpu(), os.path.join(result_dir, "c.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("layout,chunks", [("nk", 4), ("kn", 1)])
+def test_row_sharded_gemm_nccl(tmp_path, layout, chunks):
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(world, 8)
+    M, N, K = 4099, 1000, 520  # ragged panels and a ragged last chunk
+    mp.spawn(_worker, args=(world, _free_port(), M, N, K, layout, chunks, str(tmp_path)), nprocs=world, join=True)
+    c = torch.load(os.path.join(tmp_path, "c.pt"))
+    from oracle import oracle as o
+    from tests._util import bits, check_parity, uniform_bf16
+    a = uniform_bf16((M, K), 11)
+    b = uniform_bf16((N, K) if layout == "nk" else (K, N), 12)
+    ref = o.gemm_bf16(bits(a), bits(b), 0 if layout == "nk" else 1)
+    c32 = o.gemm_f32acc(bits(a), bits(b), 0 if layout == "nk" else 1).astype(np.float64)
+    check_parity(bits(c), c32, ref, ctx=f"row-sharded x{world} {layout}")

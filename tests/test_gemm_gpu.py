@@ -198,3 +198,89 @@ def test_strided_views_and_errors():
         b200_gemm.gemm(base[:, 1:321], b)  # 2-byte offset: not 16-byte aligned
     with pytest.raises(ValueError):
         b200_gemm.gemm(a, b.t())  # not row-major
+
+
+@pytest.fixture
+def forced_kernel():
+    """Yields a setter for the kernel override and restores automatic selection afterwards."""
+    yield b200_gemm.set_kernel
+    b200_gemm.set_kernel("auto")
+
+
+FORCE_SHAPES = [(1, 8, 8), (5, 3, 7), (17, 129, 70), (100, 300, 136), (128, 256, 1000), (129, 257, 65),
+                (300, 520, 200)]
+
+
+@pytest.mark.parametrize("kernel", ["single", "pair", "skinny"])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("shape", FORCE_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_every_kernel_path_vs_oracle(shape, layout, kernel, forced_kernel):
+    """Each of the three kernels computes the same product on ragged shapes."""
+    M, N, K = shape
+    if kernel == "skinny" and M > 128:
+        forced_kernel("skinny")
+        a = torch.zeros((M, 8), dtype=torch.bfloat16, device=DEV)
+        with pytest.raises(b200_gemm.B200GemmError):
+            b200_gemm.matmul(a, torch.zeros((8, 8), dtype=torch.bfloat16, device=DEV))
+        return
+    forced_kernel(kernel)
+    a, b, b_nk = _make(M, N, K, layout, seed=M + 3 * N + 7 * K)
+    c = _run(a, b, layout)
+    c_or = o.gemm_bf16(bits(a), bits(b_nk), 0)
+    c64, _ = o.gemm_f64(bits(a), bits(b_nk), 0)
+    check_parity(bits(c), c64, c_or, ctx=f"{shape} {layout} {kernel}")
+
+
+SKINNY_CFG = [(m, n, k) for m in (16, 64, 128) for (n, k) in ((4096, 4096), (14336, 4096), (4096, 14336))]
+
+
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+@pytest.mark.parametrize("shape", SKINNY_CFG, ids=lambda s: "x".join(map(str, s)))
+def test_baseline_skinny_configs_vs_oracle(shape, layout):
+    """A ~ N(0,1), B ~ N(0, 1/K), every element against the oracle."""
+    M, N, K = shape
+    a = normal_bf16((M, K), M + N)
+    b_nk = normal_bf16((N, K), K + 1, std=K ** -0.5)
+    b = b_nk if layout == "nk" else b_nk.t().contiguous()
+    c = b200_gemm.gemm(a.to(DEV), b.to(DEV), b_layout=layout)
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    c_or = o.gemm_bf16(bits(a), bits(b_nk), 0)
+    c32 = o.gemm_f32acc(bits(a), bits(b_nk), 0).astype(np.float64)
+    check_parity(bits(c), c32, c_or, ctx=f"{shape} {layout}")
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 31, 48, 65, 127, 128])
+def test_skinny_split_k_vs_oracle(M):
+    """Small M with K long enough for a multi-CTA cluster split and a ragged last split."""
+    N, K = 1000, 3000
+    a = uniform_bf16((M, K), M)
+    b = uniform_bf16((N, K), M + 1)
+    c = _run(a, b, "nk")
+    c_or = o.gemm_bf16(bits(a), bits(b), 0)
+    c64, _ = o.gemm_f64(bits(a), bits(b), 0)
+    check_parity(bits(c), c64, c_or, ctx=f"M={M}")
+
+
+def test_device_wait_timeout_is_reported_and_context_survives():
+    """A bounded device wait on a barrier nothing arrives at gives up after its
+    limit; the host reads B200_ERR_DEVICE_TIMEOUT and the GPU keeps working."""
+    import ctypes
+    import time
+    from b200_gemm import _lib
+    lib = _lib.load()
+    assert b200_gemm.check_status() == 0
+    s = torch.cuda.current_stream()
+    t0 = time.time()
+    assert lib.b200_gemm_selftest_wait_timeout(200_000_000, ctypes.c_void_p(s.cuda_stream)) == 0  # 0.2 s
+    bits_ = ctypes.c_uint32(0)
+    rc = lib.b200_gemm_status(ctypes.c_void_p(s.cuda_stream), ctypes.byref(bits_))
+    dt = time.time() - t0
+    assert rc == _lib.B200_ERR_DEVICE_TIMEOUT and bits_.value != 0
+    assert 0.15 < dt < 5.0, dt
+    assert b200_gemm.check_status() == 0  # the status word was cleared by the read
+    a = uniform_bf16((256, 128), 1).to(DEV)
+    b = uniform_bf16((64, 128), 2).to(DEV)
+    c = b200_gemm.matmul(a, b)
+    torch.cuda.synchronize()
+    assert np.mean(bits(c) != o.gemm_bf16(bits(a.cpu()), bits(b.cpu()), 0)) < 0.01
