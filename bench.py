@@ -246,11 +246,17 @@ def time_config(M, N, K, layout, dist_kind, b200_gemm, target_ms=250.0, warmup=1
     def ours(i):
         b200_gemm.gemm(A[i % R], B[i % R], b_layout=layout, out=C[i % R])
 
+    def ours_splitk(i):
+        b200_gemm.gemm(A[i % R], B[i % R], b_layout=layout, out=C[i % R], split_k=True)
+
     def cublas(i):
         torch.matmul(A[i % R], B[i % R] if layout == "kn" else B[i % R].t(), out=C[i % R])
 
     res = {}
-    for name, fn in (("b200", ours), ("cublas", cublas)):
+    variants = [("b200", ours), ("cublas", cublas)]
+    if b200_gemm.ops.workspace_bytes(M, N, K, layout) > 0:
+        variants.insert(1, ("b200_split_k", ours_splitk))
+    for name, fn in variants:
         if name == "cublas" and not with_cublas:
             continue
         for i in range(warmup):
@@ -321,6 +327,9 @@ def run_sweep(args) -> int:
                     "bound": "hbm" if hbm_bound else "tensor",
                     "frac": round(gbs / peaks["hbm_gbs"] if hbm_bound else tf / peaks["burst"], 4),
                     "peak_source": peaks["source"], "timing": "graph replay" if (not args.no_graph and t["b200"] < 1.0) else "direct launches"}
+            if "b200_split_k" in t:
+                line["split_k_tail_ms"] = round(t["b200_split_k"], 5)
+                line["split_k_tail_tflops"] = round(flops / (t["b200_split_k"] / 1e3) / 1e12, 1)
             if "cublas" in t:
                 line["cublas_ms"] = round(t["cublas"], 5)
                 line["speedup_vs_cublas"] = round(t["cublas"] / t["b200"], 3)

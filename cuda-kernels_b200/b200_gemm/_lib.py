@@ -34,6 +34,12 @@ _SIGNATURES = {
                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_int, ctypes.c_void_p]),
+    "b200_gemm_bf16_ws": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "b200_gemm_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                                 ctypes.POINTER(ctypes.c_size_t)]),
     "b200_gemm_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "b200_gemm_set_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "b200_gemm_set_kernel": (ctypes.c_int, [ctypes.c_int]),

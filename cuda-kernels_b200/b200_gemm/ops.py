@@ -39,8 +39,16 @@ def _check_operand(name: str, t: torch.Tensor) -> None:
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.Tensor | None = None,
-         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """C = A @ op(B) in bf16 with fp32 accumulation on a B200 (sm_100a)."""
+         stream: torch.cuda.Stream | None = None, split_k: bool = False) -> torch.Tensor:
+    """C = A @ op(B) in bf16 with fp32 accumulation on a B200 (sm_100a).
+
+    split_k=True lets the tiles of the last, partial wave be split along K
+    across CTA pairs (b200_gemm_bf16_ws), which shortens that wave.  It changes
+    the fp32 summation order of those tiles: results stay within the bf16
+    tolerance of the exact product but are no longer bit-identical to a
+    sequential-K GEMM such as cuBLAS (near-zero outputs can differ by more than
+    torch.testing.assert_close's default atol).  The default keeps the
+    sequential K order of the reference kernels."""
     if b_layout not in _LAYOUTS:
         raise ValueError(f"b_layout must be 'nk' or 'kn', got {b_layout!r}")
     _check_operand("A", a)
@@ -63,16 +71,40 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.T
         if out.device != a.device:
             raise ValueError("out must be on the same device as A")
     lib = _lib.load()
-    with torch.cuda.device(a.device):
+    layout = _LAYOUTS[b_layout]
+    dev_index = a.device.index
+    switch = dev_index != torch.cuda.current_device()
+    if switch:
+        prev = torch.cuda.current_device()
+        torch.cuda.set_device(dev_index)
+    try:
         s = stream if stream is not None else torch.cuda.current_stream(a.device)
-        rc = lib.b200_gemm_bf16(
+        # Split-K workspace for the last wave of tiles (0 bytes when the shape
+        # does not need it); torch's caching allocator makes this cheap and
+        # stream-safe, so concurrent calls never share a workspace.
+        ws_bytes = workspace_bytes(M, N, K, b_layout) if split_k else 0
+        ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=a.device) if ws_bytes else None
+        ws_ptr = ((ws.data_ptr() + 255) // 256 * 256) if ws is not None else None
+        rc = lib.b200_gemm_bf16_ws(
             ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()),
             M, N, K,
             max(a.stride(0), 1), max(b.stride(0), 1), max(out.stride(0), 1),
-            _LAYOUTS[b_layout], ctypes.c_void_p(s.cuda_stream))
+            layout, ctypes.c_void_p(ws_ptr), ws_bytes, ctypes.c_void_p(s.cuda_stream))
+    finally:
+        if switch:
+            torch.cuda.set_device(prev)
     if rc != _lib.B200_OK:
         raise B200GemmError(rc, f"M={M} N={N} K={K} b_layout={b_layout}")
     return out
+
+
+def workspace_bytes(M: int, N: int, K: int, b_layout: str = "nk") -> int:
+    """Split-K workspace (bytes) b200_gemm_bf16_ws wants for this shape on the current device."""
+    n = ctypes.c_size_t(0)
+    rc = _lib.load().b200_gemm_workspace_bytes(M, N, K, _LAYOUTS[b_layout], ctypes.byref(n))
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc)
+    return n.value
 
 
 def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:

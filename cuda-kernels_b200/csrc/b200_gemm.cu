@@ -11,7 +11,9 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <chrono>
 #include <cstdint>
+#include <random>
 #include <cstring>
 #include <mutex>
 
@@ -62,7 +64,53 @@ struct DeviceState {
   int max_pairs = 0;  // co-resident 2-CTA clusters of the pair kernel
   uint32_t* status_ptr = nullptr;
   uint64_t timeout_ns = kDefaultTimeoutNs;
+  std::atomic<uint32_t> epoch{0};  // split-K hand-off counter, one step per launch
 };
+
+// Split-K plan for the pair kernel's last, partial wave of tiles (see
+// GemmParams): the `rem` tiles left after the full waves are each split into
+// `parts` K ranges so that rem x parts work items fill the pairs again.
+struct SplitPlan {
+  int32_t first, parts, kpp, work;
+  size_t partial_bytes, flag_bytes;
+  size_t bytes() const { return partial_bytes + flag_bytes; }
+};
+constexpr size_t kWsAlign = 256;
+
+uint32_t process_salt() {
+  static const uint32_t salt = [] {
+    std::random_device rd;
+    uint32_t v = rd() ^ (uint32_t)std::chrono::steady_clock::now().time_since_epoch().count();
+    return v == 0 ? 0x9e3779b9u : v;
+  }();
+  return salt;
+}
+
+SplitPlan plan_split(int64_t tiles, int32_t num_k_blk, int max_pairs, int bn) {
+  SplitPlan sp{(int32_t)tiles, 1, num_k_blk, (int32_t)tiles, 0, 0};
+  if (max_pairs <= 0) return sp;
+  const int64_t rem = tiles % max_pairs;
+  if (rem == 0) return sp;
+  int64_t parts = max_pairs / rem;
+  if (parts > 8) parts = 8;
+  // Each part must keep enough K to amortise the partial hand-off (a 256 KB
+  // fp32 tile written and read back per part); measured on B200: 4 K-blocks
+  // per part made 1024^3 1.7x slower, 32 per part made 4096^3 faster.
+  constexpr int32_t kMinKbPerPart = 16;
+  if (parts > num_k_blk / kMinKbPerPart) parts = num_k_blk / kMinKbPerPart;
+  if (parts < 2) return sp;
+  const int32_t kpp = (int32_t)((num_k_blk + parts - 1) / parts);
+  parts = (num_k_blk + kpp - 1) / kpp;
+  if (parts < 2) return sp;
+  sp.first = (int32_t)(tiles - rem);
+  sp.parts = (int32_t)parts;
+  sp.kpp = kpp;
+  sp.work = (int32_t)(sp.first + rem * parts);
+  const size_t slots = (size_t)rem * (size_t)(parts - 1) * 2;  // 2 CTAs per pair
+  sp.partial_bytes = (slots * (size_t)b200::kBM * (size_t)bn * sizeof(float) + kWsAlign - 1) / kWsAlign * kWsAlign;
+  sp.flag_bytes = (slots * sizeof(uint64_t) + kWsAlign - 1) / kWsAlign * kWsAlign;
+  return sp;
+}
 
 DeviceState g_dev[kMaxDevices];
 
@@ -267,8 +315,10 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
 
 }  // namespace
 
-extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                              int64_t ldb, int64_t ldc, int b_layout, void* stream_) {
+namespace {
+
+int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+              int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes, void* stream_) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
   if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
   const int64_t kLim = 0x7fffffffLL;
@@ -337,13 +387,39 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
   p.status = st->status_ptr;
 
   if (!use_pair) {
+    p.sk_first = p.num_work = p.num_tiles;
+    p.sk_parts = 1;
+    p.sk_kpp = p.num_k_blk;
     const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
     auto kern = p.b_mn_major ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>
                              : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>;
     kern<<<grid, b200::kNumThreads, b200::SmemPlan<kBN, kStages>::kAllocBytes, stream>>>(tmA, tmB, tmC, p);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
-  const int pairs = (int)(tiles < st->max_pairs ? tiles : st->max_pairs);
+  p.sk_first = p.num_tiles;
+  p.sk_parts = 1;
+  p.sk_kpp = p.num_k_blk;
+  p.num_work = p.num_tiles;
+  if (workspace != nullptr) {
+    const SplitPlan sp = plan_split(tiles, p.num_k_blk, st->max_pairs, kPairBN);
+    if (sp.parts >= 2 && workspace_bytes >= sp.bytes() &&
+        (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) == 0) {
+      p.sk_first = sp.first;
+      p.sk_parts = sp.parts;
+      p.sk_kpp = sp.kpp;
+      p.num_work = sp.work;
+      p.workspace = static_cast<float*>(workspace);
+      p.flags = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + sp.partial_bytes);
+      // The workspace is not initialised: a flag may hold anything.  A
+      // 64-bit tag with a random per-process half makes an accidental match
+      // with leftover memory contents practically impossible; the counter
+      // half keeps consecutive launches apart.
+      const uint32_t n = st->epoch.fetch_add(1, std::memory_order_relaxed) + 1;
+      p.epoch = ((uint64_t)process_salt() << 32) | (uint64_t)n;
+    }
+  }
+  const int64_t work = p.num_work;
+  const int pairs = (int)(work < st->max_pairs ? work : st->max_pairs);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -360,6 +436,37 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
       p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>, tmA, tmB, tmC, p)
                    : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>, tmA, tmB, tmC, p);
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                       int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream) {
+  return gemm_impl(A, B, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
+}
+
+extern "C" B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                          int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (workspace == nullptr && workspace_bytes != 0) return B200_ERR_INVALID_ARG;
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) != 0) return B200_ERR_ALIGNMENT;
+  return gemm_impl(A, B, C, M, N, K, lda, ldb, ldc, b_layout, workspace, workspace_bytes, stream);
+}
+
+extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {
+  if (bytes == nullptr || M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
+  if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
+  *bytes = 0;
+  DeviceState* st = nullptr;
+  const int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  const int force = g_force_kernel.load(std::memory_order_relaxed);
+  const bool pair = force == kForcePair || (force == kForceAuto && M > 128);
+  if (!pair || M == 0 || N == 0 || K == 0) return B200_OK;
+  const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
+  const SplitPlan sp = plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st->max_pairs, kPairBN);
+  if (sp.parts >= 2) *bytes = sp.bytes();
+  return B200_OK;
 }
 
 extern "C" B200_API int b200_gemm_status(void* stream_, uint32_t* device_bits) {

@@ -49,9 +49,18 @@ struct GemmParams {
   int32_t num_tiles;
   int32_t group_m;       // tiles are rasterised in groups of `group_m` M-blocks
   uint32_t b_mn_major;   // 0: B is [N,K] (K contiguous); 1: B is [K,N] (N contiguous)
-  uint32_t pad_;
+  // Split-K tail (pair kernel only).  Work items [0, sk_first) are whole tiles
+  // 0 .. sk_first-1.  Each tile from sk_first on is split into sk_parts
+  // ranges of sk_kpp K-blocks, one work item per range; parts 0..sk_parts-2
+  // write fp32 partial tiles to `workspace` and publish `epoch` in `flags`;
+  // the last part adds the partials (in part order) and stores C.  Without a
+  // split: sk_first = num_work = num_tiles.
+  int32_t sk_first, sk_parts, sk_kpp, num_work;
+  uint64_t epoch;        // per-launch tag: random per-process high half, launch counter low half
   uint64_t timeout_ns;   // limit for every mbarrier wait
   uint32_t* status;      // device status word (DeviceStatus bits), OR-ed on failure
+  float* workspace;      // [split tiles][sk_parts-1][2 CTAs][BN/4][128][4] fp32
+  uint64_t* flags;       // [split tiles][sk_parts-1][2 CTAs]
 };
 
 template <int BN, int STAGES>
@@ -80,6 +89,32 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb,
   const int r = t - g * tiles_per_group;
   mb = first_m + r % gm;
   nb = r / gm;
+}
+
+struct WorkItem {
+  int mb, nb;    // tile coordinates
+  int part;      // -1: whole K range; otherwise the split-K part index
+  int kb0, kb1;  // K-block range [kb0, kb1)
+  int split;     // index of the split tile (w.r.t. sk_first), or -1
+};
+
+__device__ __forceinline__ WorkItem work_item(int w, const GemmParams& p) {
+  WorkItem r;
+  if (w < p.sk_first) {
+    tile_coords(w, p, r.mb, r.nb);
+    r.part = -1;
+    r.kb0 = 0;
+    r.kb1 = p.num_k_blk;
+    r.split = -1;
+  } else {
+    const int u = w - p.sk_first;
+    r.split = u / p.sk_parts;
+    r.part = u - r.split * p.sk_parts;
+    tile_coords(p.sk_first + r.split, p, r.mb, r.nb);
+    r.kb0 = r.part * p.sk_kpp;
+    r.kb1 = min(r.kb0 + p.sk_kpp, p.num_k_blk);
+  }
+  return r;
 }
 
 __device__ __forceinline__ void raise_status(const GemmParams& p, volatile uint32_t* abort_flag, uint32_t code) {

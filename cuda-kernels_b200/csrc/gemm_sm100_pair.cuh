@@ -123,12 +123,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
-        int mb, nb;
-        tile_coords(t, p, mb, nb);
-        const int row0 = mb * kPairBM + (int)rank * kBM;
-        const int col0 = nb * BN + (int)rank * kHalfN;
-        for (int kb = 0; kb < p.num_k_blk; ++kb) {
+      for (int w = pair; w < p.num_work && ok; w += num_pairs) {
+        const WorkItem wk = work_item(w, p);
+        const int row0 = wk.mb * kPairBM + (int)rank * kBM;
+        const int col0 = wk.nb * BN + (int)rank * kHalfN;
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
             ok = false;
             break;
@@ -188,14 +187,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+      for (int w = pair; w < p.num_work && ok; w += num_pairs) {
+        const WorkItem wk = work_item(w, p);
         if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < p.num_k_blk; ++kb) {
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, abort_flag)) {
             ok = false;
             break;
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint64_t bd = b_desc0 + (uint64_t)((stage * Plan::kBBytes) >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            umma_bf16_pair(d_tmem, ad + 2u * k, bd + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16_pair(d_tmem, ad + 2u * k, bd + kBStep * k, idesc, (kb != wk.kb0 || k != 0) ? 1u : 0u);
           }
           // Stage `stage` is free in both CTAs once these MMAs have read it.
           umma_commit_pair_both(empty_bar(stage));
@@ -234,17 +234,35 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
-    for (int t = pair; t < p.num_tiles; t += num_pairs) {
-      int mb, nb;
-      tile_coords(t, p, mb, nb);
+    for (int w = pair; w < p.num_work; w += num_pairs) {
+      const WorkItem wk = work_item(w, p);
       const bool got = mbar_wait(accf_bar(acc), acc_phase, p.timeout_ns, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {
+      // All four epilogue warps take the same decision (they meet at named
+      // barriers below, so none may leave the loop alone).
+      if (!named_bar_and(2, kEpiWarps * 32, got)) {
         if (lane == 0) raise_status(p, abort_flag, kDevTimeoutEpilogue);
         break;
       }
       tc_fence_after();
       const uint32_t t_row = tmem_base + tmem_lane + (uint32_t)(acc * BN);
-      const int row = mb * kPairBM + (int)rank * kBM + q * kEpiRowsPerWarp;
+      const int row_local = q * kEpiRowsPerWarp + (int)lane;  // row of this CTA's 128-row half
+      const int row = wk.mb * kPairBM + (int)rank * kBM + q * kEpiRowsPerWarp;
+      // Split-K slots of this CTA: partial of part j lives at slot (split, j, rank).
+      const bool sk_writer = wk.part >= 0 && wk.part < p.sk_parts - 1;
+      const bool sk_finisher = wk.part >= 0 && wk.part == p.sk_parts - 1;
+      auto slot_index = [&](int j) { return (wk.split * (p.sk_parts - 1) + j) * 2 + (int)rank; };
+      if (sk_finisher) {
+        // Wait until every earlier part of this tile has published its partial.
+        if (warp == 2 && lane == 0) {
+          for (int j = 0; j < p.sk_parts - 1; ++j) {
+            if (!wait_flag_eq(p.flags + slot_index(j), p.epoch, p.timeout_ns)) {
+              raise_status(p, abort_flag, kDevTimeoutSplitK);
+              break;
+            }
+          }
+        }
+        named_bar_sync(1, kEpiWarps * 32);
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / kEpiCols; ++c) {
         uint32_t r0[32], r1[32];
@@ -257,6 +275,33 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(mapa_shared(acce_bar(acc), 0));
         }
+        if (sk_writer) {
+          // fp32 partial, layout [BN/4][128 rows][4]: a warp's 32 rows of one
+          // 4-column group are 512 contiguous bytes.
+          float* dst = p.workspace + (size_t)slot_index(wk.part) * (size_t)(kBM * BN);
+#pragma unroll
+          for (int g = 0; g < 16; ++g) {
+            const uint32_t* src = g < 8 ? &r0[g * 4] : &r1[(g - 8) * 4];
+            st_global_v4(dst + ((size_t)(c * 16 + g) * kBM + row_local) * 4, __uint_as_float(src[0]),
+                         __uint_as_float(src[1]), __uint_as_float(src[2]), __uint_as_float(src[3]));
+          }
+          continue;
+        }
+        if (sk_finisher) {
+          // Add the earlier parts' partials in part order (deterministic).
+          for (int j = 0; j < p.sk_parts - 1; ++j) {
+            const float* src = p.workspace + (size_t)slot_index(j) * (size_t)(kBM * BN);
+#pragma unroll
+            for (int g = 0; g < 16; ++g) {
+              const float4 v = ld_global_cg_v4(src + ((size_t)(c * 16 + g) * kBM + row_local) * 4);
+              uint32_t* d = g < 8 ? &r0[g * 4] : &r1[(g - 8) * 4];
+              d[0] = __float_as_uint(__uint_as_float(d[0]) + v.x);
+              d[1] = __float_as_uint(__uint_as_float(d[1]) + v.y);
+              d[2] = __float_as_uint(__uint_as_float(d[2]) + v.z);
+              d[3] = __float_as_uint(__uint_as_float(d[3]) + v.w);
+            }
+          }
+        }
         const uint32_t buf = sC + (uint32_t)((slot * 2 + sbuf) * kEpiBufBytes);
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
@@ -264,24 +309,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t* src = (j < 4) ? &r0[j * 8] : &r1[(j - 4) * 8];
-          uint32_t w[4];
+          uint32_t wv[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(src[2 * e]), __uint_as_float(src[2 * e + 1]));
-            w[e] = *reinterpret_cast<uint32_t*>(&h);
+            wv[e] = *reinterpret_cast<uint32_t*>(&h);
           }
           const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                       "r"(w[3])
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(wv[0]), "r"(wv[1]), "r"(wv[2]),
+                       "r"(wv[3])
                        : "memory");
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf, nb * BN + c * kEpiCols, row);
+          tma_store_2d(&tmC, buf, wk.nb * BN + c * kEpiCols, row);
           bulk_commit_group();
         }
         sbuf ^= 1;
+      }
+      if (sk_writer) {
+        // Publish: every epilogue thread's partial stores happen-before the
+        // release of the flag (barrier, then a release store at GPU scope).
+        named_bar_sync(1, kEpiWarps * 32);
+        if (warp == 2 && lane == 0) st_release_gpu(p.flags + slot_index(wk.part), p.epoch);
       }
       if (++acc == kAccBufs) {
         acc = 0;

@@ -26,6 +26,7 @@ enum DeviceStatus : uint32_t {
   kDevTimeoutEpilogue = 4u,   // epilogue gave up waiting for an accumulator
   kDevTimeoutDrain = 8u,      // teardown gave up waiting for in-flight copies
   kDevWrongArch = 16u,        // a copy of the kernel built without sm_100a features ran
+  kDevTimeoutSplitK = 32u,    // the last split-K part gave up waiting for a partial
 };
 
 // Kernel bodies use tcgen05/TMA, which exist only in the sm_100a feature set.
@@ -114,6 +115,61 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
     if (abort_flag != nullptr && *abort_flag != 0u) return false;
     if (globaltimer_ns() - t0 > timeout_ns) return false;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Global-memory flags between CTAs of one kernel (split-K hand-off)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_gpu(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *flag == value; false after timeout_ns.
+__device__ __forceinline__ bool wait_flag_eq(const uint64_t* flag, uint64_t value, uint64_t timeout_ns) {
+  if (ld_acquire_gpu(flag) == value) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (ld_acquire_gpu(flag) == value) return true;
+      __nanosleep(64);
+    }
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+// Named barrier for a subset of the CTA's warps (id != 0).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// Barrier over `threads` threads of the CTA that also ANDs a predicate across
+// them: every participant gets the same answer.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+// L2-only load (bypasses L1, which is not coherent with other SMs' writes).
+__device__ __forceinline__ float4 ld_global_cg_v4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
 }
 
 // ---------------------------------------------------------------------------

@@ -24,6 +24,7 @@
 #ifndef B200_GEMM_H_
 #define B200_GEMM_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -72,6 +73,34 @@ extern "C" {
  */
 B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                    int64_t ldb, int64_t ldc, int b_layout, void* stream);
+
+/*
+ * Same product as b200_gemm_bf16, with a caller-provided device workspace.
+ * When the tiles of a problem do not fill the last wave of the GPU's CTA
+ * pairs, the tiles of that wave are split along K across several pairs; the
+ * partial sums meet in `workspace` (fp32 partial tiles plus hand-off flags).
+ * Needs workspace_bytes >= b200_gemm_workspace_bytes(...) and a 256-byte
+ * aligned pointer; with less (or NULL, 0) it runs without the split, exactly
+ * like b200_gemm_bf16.  The workspace needs no initialisation; calls that may
+ * run at the same time on the GPU must not share a workspace.  Results are
+ * deterministic (partials are added in a fixed order) and within the bf16
+ * tolerance of the exact product, but split tiles sum K in a different order
+ * than b200_gemm_bf16, cuBLAS or the reference kernels, so near-zero outputs
+ * (cancellation) can differ from theirs in the last bits.  b200_gemm_bf16 is
+ * the sequential-K default.
+ * No reference counterpart: the reference launches one CTA per tile
+ * (bf16_matmul/matmul_v8_tuned.cu:255-256) and has no tail handling.
+ */
+B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/*
+ * Workspace b200_gemm_bf16_ws wants for this shape on the current device
+ * (0 when it would not split; at most ~19 MB on a B200).  Depends on the
+ * device's SM count and on b200_gemm_set_kernel.
+ */
+B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes);
 
 /*
  * Waits for `stream`, then reads and clears the current device's status word.

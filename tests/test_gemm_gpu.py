@@ -284,3 +284,67 @@ def test_device_wait_timeout_is_reported_and_context_survives():
     c = b200_gemm.matmul(a, b)
     torch.cuda.synchronize()
     assert np.mean(bits(c) != o.gemm_bf16(bits(a.cpu()), bits(b.cpu()), 0)) < 0.01
+
+
+def _raw_gemm(a, b, c, layout, ws=None, ws_bytes=0):
+    import ctypes
+    from b200_gemm import _lib
+    lib = _lib.load()
+    M, K = a.shape
+    N = c.shape[1]
+    s = torch.cuda.current_stream().cuda_stream
+    if ws is None:
+        return lib.b200_gemm_bf16(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, a.stride(0), b.stride(0),
+                                  c.stride(0), 0 if layout == "nk" else 1, ctypes.c_void_p(s))
+    return lib.b200_gemm_bf16_ws(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, a.stride(0), b.stride(0),
+                                 c.stride(0), 0 if layout == "nk" else 1, ctypes.c_void_p(ws), ws_bytes,
+                                 ctypes.c_void_p(s))
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1024, 1024, 8192), (640, 2560, 2056), (300, 520, 4100),
+                                   (129, 257, 1030), (5000, 4096, 4096)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_split_k_tail_matches_oracle_and_is_deterministic(shape, layout):
+    """The last wave's tiles split along K across pairs (b200_gemm_bf16_ws):
+    same product as without the split (both against the oracle), and two
+    calls give identical bits (partials are added in a fixed order)."""
+    M, N, K = shape
+    ws_bytes = b200_gemm.ops.workspace_bytes(M, N, K, layout)
+    assert ws_bytes > 0, "shape chosen to exercise the split-K tail"
+    a, b, b_nk = _make(M, N, K, layout, seed=M + N + K)
+    ad, bd = _padded(a), _padded(b)  # row pitches rounded up to 8 elements
+    ws = torch.empty(max(ws_bytes, 1) + 256, dtype=torch.uint8, device=DEV)
+    ws_ptr = (ws.data_ptr() + 255) // 256 * 256
+
+    def out():
+        return torch.zeros((M, _pad8(N)), dtype=torch.bfloat16, device=DEV)[:, :N]
+    c_split, c_split2, c_plain = out(), out(), out()
+    assert _raw_gemm(ad, bd, c_split, layout, ws_ptr, ws_bytes) == 0
+    ws.fill_(0xAB)  # leftover bytes in the workspace must not matter
+    assert _raw_gemm(ad, bd, c_split2, layout, ws_ptr, ws_bytes) == 0
+    assert _raw_gemm(ad, bd, c_plain, layout) == 0
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    assert torch.equal(c_split, c_split2)
+    rows = _rows(M, 64, K) if M > 512 else torch.arange(M)
+    for c, ctx in ((c_split, "split"), (c_plain, "plain")):
+        _sampled_parity(a, b_nk, c.cpu(), rows, ctx=f"{shape} {layout} {ctx}")
+
+
+def test_split_k_workspace_arguments():
+    from b200_gemm import _lib
+    M = N = K = 4096
+    ws_bytes = b200_gemm.ops.workspace_bytes(M, N, K, "nk")
+    assert 0 < ws_bytes < 32 << 20
+    a = uniform_bf16((M, K), 1).to(DEV)
+    b = uniform_bf16((N, K), 2).to(DEV)
+    ws = torch.empty(ws_bytes + 512, dtype=torch.uint8, device=DEV)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    c_small = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    c_ref = torch.empty_like(c_small)
+    assert _raw_gemm(a, b, c_small, "nk", base, ws_bytes - 1) == 0   # too small: runs without the split
+    assert _raw_gemm(a, b, c_ref, "nk") == 0
+    assert _raw_gemm(a, b, c_ref, "nk", base + 16, ws_bytes) == _lib.B200_ERR_ALIGNMENT
+    torch.cuda.synchronize()
+    assert torch.equal(c_small, c_ref)
+    assert b200_gemm.ops.workspace_bytes(64, 4096, 4096, "nk") == 0  # skinny kernel: no split-K tail
