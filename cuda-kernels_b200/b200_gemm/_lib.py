@@ -19,6 +19,7 @@ B200_ERR_CUDA = 4
 B200_ERR_TENSOR_MAP = 5
 B200_ERR_DEVICE_TIMEOUT = 6
 B200_ERR_TOO_LARGE = 7
+B200_ERR_SCRATCH_LIMIT = 8
 
 B200_B_NK = 0
 B200_B_KN = 1
@@ -38,6 +39,10 @@ _SIGNATURES = {
                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "b200_gemm_bf16_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int, ctypes.c_void_p]),
     "b200_gemm_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                                                  ctypes.POINTER(ctypes.c_size_t)]),
     "b200_gemm_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),

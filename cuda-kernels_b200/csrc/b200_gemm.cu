@@ -543,8 +543,63 @@ extern "C" B200_API const char* b200_gemm_strerror(int code) {
     case B200_ERR_TENSOR_MAP: return "tensor map encode failed";
     case B200_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
     case B200_ERR_TOO_LARGE: return "dimension too large";
+    case B200_ERR_SCRATCH_LIMIT: return "split-K scratch needed exceeds the 16 MiB static buffer of b200_gemm_bf16_noalloc";
     default: return "unknown error";
   }
 }
 
 extern "C" B200_API const char* b200_gemm_version(void) { return "b200_gemm 0.1.0 sm_100a"; }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the split-K GEMM.
+//
+// Some callers cannot allocate device memory at the point where they multiply:
+// a serving engine that reserves every byte of HBM at start-up and must not
+// call cudaMalloc on its request path (cudaMalloc can synchronise the device
+// and stall every stream), or a plugin whose host framework hands it raw
+// buffers but no allocator.  For them the split-K scratch lives in a static
+// device array inside this library instead of a caller workspace.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Static split-K scratch: 16 MiB, enough for any shape on a 148-SM B200
+// (at most 15.75 MiB: 73 partial 256x256 fp32 tiles plus hand-off flags).
+// Every GPU that loads this library holds it until the process exits.
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocState {
+  std::once_flag once;
+  int rc = B200_OK;
+  void* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+};
+NoAllocState g_noalloc[kMaxDevices];
+
+}  // namespace
+
+extern "C" B200_API int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                               int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream) {
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  // One-time set-up per device (runs inside the first call on that device,
+  // with that device current): the host-side name g_noalloc_scratch is not a
+  // device address, so look the address up and keep it.
+  NoAllocState& na = g_noalloc[dev];
+  std::call_once(na.once, [&] {
+    na.rc = cudaGetSymbolAddress(&na.scratch, g_noalloc_scratch) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  });
+  if (na.rc != B200_OK) return na.rc;
+  // Reject shapes whose split-K scratch would not fit the static buffer.
+  if (M > 0 && N > 0 && K > 0 && M > 128) {
+    const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
+    const SplitPlan sp = plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st->max_pairs, kPairBN);
+    if (sp.parts >= 2 && sp.bytes() > kNoAllocScratchBytes) return B200_ERR_SCRATCH_LIMIT;
+  }
+  // Nothing in the scratch needs clearing between calls: every partial tile is
+  // written in full before it is read, and the hand-off flags are matched
+  // against a tag that is new for every launch.
+  return gemm_impl(A, B, C, M, N, K, lda, ldb, ldc, b_layout, na.scratch, kNoAllocScratchBytes, stream);
+}

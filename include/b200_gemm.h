@@ -46,6 +46,7 @@ extern "C" {
 #define B200_ERR_TENSOR_MAP 5        /* cuTensorMapEncodeTiled rejected a descriptor */
 #define B200_ERR_DEVICE_TIMEOUT 6    /* a kernel wait hit its time limit (see b200_gemm_status) */
 #define B200_ERR_TOO_LARGE 7         /* a dimension exceeds 2^31-1 */
+#define B200_ERR_SCRATCH_LIMIT 8     /* b200_gemm_bf16_noalloc: split-K scratch beyond its 16 MiB static buffer */
 
 /* Layout of the B operand. */
 #define B200_B_NK 0 /* B stored [N,K] row-major (K contiguous): C = A * B^T.  The reference's layout. */
@@ -101,6 +102,28 @@ B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M,
  * device's SM count and on b200_gemm_set_kernel.
  */
 B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes);
+
+/*
+ * Same product as b200_gemm_bf16_ws, for callers that cannot allocate device
+ * memory when they multiply (a serving engine that reserves all of HBM at
+ * start-up and keeps cudaMalloc off its request path, or a plugin whose host
+ * hands it buffers but no allocator).  It allocates nothing: its split-K
+ * scratch is a 16 MiB static array inside this library, held by every GPU
+ * that loads the library until the process exits.  Shapes that would need
+ * more scratch than that are rejected with B200_ERR_SCRATCH_LIMIT (none do
+ * on a 148-SM B200).
+ *
+ * The first call on each device also looks up the device address of that
+ * array (with that device current); make that first call before any stream
+ * capture.  Every call shares the one array, and the array keeps whatever the
+ * last call left in it, which is harmless (partials are fully rewritten and
+ * hand-off flags carry a per-launch tag) — but calls whose kernels can overlap
+ * on the GPU (other streams, other host threads) race on it: issue them on
+ * one stream, or use b200_gemm_bf16_ws with separate workspaces.
+ * No counterpart in the reference, which allocates nothing of its own.
+ */
+B200_API int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                    int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream);
 
 /*
  * Waits for `stream`, then reads and clears the current device's status word.
