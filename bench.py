@@ -388,6 +388,25 @@ def run_rowshard(args) -> int:
     return 0
 
 
+def run_shape(args) -> int:
+    """--shape M,N,K: time one GEMM shape (ours, and cuBLAS unless --no-cublas); one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    import b200_gemm
+    M, N, K = (int(x) for x in args.shape.split(","))
+    t = time_config(M, N, K, args.layout, args.dist, b200_gemm, target_ms=args.target_ms,
+                    with_cublas=not args.no_cublas, use_graph=not args.no_graph)
+    flops = 2.0 * M * N * K
+    nbytes = 2.0 * (M * K + K * N + M * N)
+    line = {"config": {"M": M, "N": N, "K": K, "b_layout": args.layout, "data": args.dist},
+            "ms": round(t["b200"], 5), "tflops": round(flops / (t["b200"] / 1e3) / 1e12, 1),
+            "gbs": round(nbytes / (t["b200"] / 1e3) / 1e9, 1)}
+    if "cublas" in t:
+        line["cublas_ms"] = round(t["cublas"], 5)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -403,12 +422,17 @@ def main(argv=None) -> int:
     ap.add_argument("--sweep", action="store_true", help="time every single-GPU BASELINE config (one line each)")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="sweep: time direct launches instead of graph replay")
+    ap.add_argument("--shape", default=None, help="time one shape M,N,K (one JSON line)")
+    ap.add_argument("--dist", default="normal", choices=["normal", "uniform"])
+    ap.add_argument("--target-ms", type=float, default=250.0)
     ap.add_argument("--rowshard", action="store_true", help="BASELINE config 5: row-sharded 131072x8192x8192")
     ap.add_argument("--rowshard-m", type=int, default=131072)
     ap.add_argument("--chunks", type=int, default=4)
     args = ap.parse_args(argv)
     if args.rowshard:
         return run_rowshard(args)
+    if args.shape:
+        return run_shape(args)
     if args.sweep:
         return run_sweep(args)
     if args.warmup < 3:

@@ -295,17 +295,19 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   p.status = st.status_ptr;
 
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3((unsigned)splits, (unsigned)n_tiles, 1);
   cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
   cfg.dynamicSmemBytes = Plan::kAllocBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e =
       b_layout == B200_B_KN
           ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, true>, tmB, tmA, tmC, p)
@@ -393,8 +395,17 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
     auto kern = p.b_mn_major ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>
                              : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>;
-    kern<<<grid, b200::kNumThreads, b200::SmemPlan<kBN, kStages>::kAllocBytes, stream>>>(tmA, tmB, tmC, p);
-    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
+    cfg.dynamicSmemBytes = b200::SmemPlan<kBN, kStages>::kAllocBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
   p.sk_first = p.num_tiles;
   p.sk_parts = 1;
@@ -421,17 +432,19 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   const int64_t work = p.num_work;
   const int pairs = (int)(work < st->max_pairs ? work : st->max_pairs);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
   cfg.dynamicSmemBytes = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e =
       p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>, tmA, tmB, tmC, p)
                    : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>, tmA, tmB, tmC, p);

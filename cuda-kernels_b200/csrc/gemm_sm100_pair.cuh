@@ -114,6 +114,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive / transaction
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Launched with programmatic stream serialisation: the prologue above ran
+  // while the previous kernel in the stream may still be finishing; wait for
+  // it before touching global memory, and let the next kernel start its own
+  // prologue as early as possible.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ---- TMA producer (both CTAs) ---------------------------------------------

@@ -118,6 +118,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while the previous kernel in the stream is still
+// running; it must call pdl_wait() before touching global memory that the
+// previous kernel may write or read.  pdl_launch_dependents() lets the next
+// such kernel start its own prologue early.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------
 // Global-memory flags between CTAs of one kernel (split-K hand-off)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void st_release_gpu(uint64_t* p, uint64_t v) {
