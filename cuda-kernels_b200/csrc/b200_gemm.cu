@@ -271,8 +271,6 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   }
   if (rc != B200_OK) return rc;
   if ((rc = encode_2d(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, b200::kBK, MPAD, true)) != B200_OK) return rc;
-  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 32, MPAD, false, false)) != B200_OK)
-    return rc;
 
   b200::SkinnyParams p{};
   p.M = (int32_t)M;
@@ -283,14 +281,23 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   if (n_tiles > 65535) return B200_ERR_TOO_LARGE;  // grid.y limit
   // Split K so that (tiles x splits) CTAs cover the SMs once, within the
   // cluster-size and shared-memory limits; no split is left without K-blocks.
-  int64_t splits = st.sm_count / n_tiles;
-  if (splits > kMaxClusterSplits) splits = kMaxClusterSplits;
-  if (splits > Plan::max_splits()) splits = Plan::max_splits();
-  if (splits > p.num_k_blk) splits = p.num_k_blk;
-  if (splits < 1) splits = 1;
+  // Split K so that tiles x splits CTAs cover the SMs once; the split count
+  // is a power of two (each CTA of a cluster owns 128/S rows of the
+  // reduction), at most 8 (portable cluster size) and at most what the
+  // reduction scratch allows.  A split may end up with no K-blocks (it then
+  // contributes zeros).
+  int64_t cap = st.sm_count / n_tiles;
+  if (cap > kMaxClusterSplits) cap = kMaxClusterSplits;
+  if (cap > Plan::max_splits()) cap = Plan::max_splits();
+  if (cap > p.num_k_blk) cap = p.num_k_blk;
+  int64_t splits = 1;
+  while (splits * 2 <= cap) splits *= 2;
   p.kb_per_split = (int32_t)((p.num_k_blk + splits - 1) / splits);
-  splits = (p.num_k_blk + p.kb_per_split - 1) / p.kb_per_split;
   p.splits = (int32_t)splits;
+  // Each owner CTA stores a [MPAD x min(32, 128/S)] block of C.
+  const uint32_t box_n = (uint32_t)(b200::kSkinnyBN / splits < 32 ? b200::kSkinnyBN / splits : 32);
+  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, box_n, MPAD, false, false)) != B200_OK)
+    return rc;
   p.timeout_ns = st.timeout_ns;
   p.status = st.status_ptr;
 

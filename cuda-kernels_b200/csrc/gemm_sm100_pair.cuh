@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         acc_phase ^= 1u;
       }
     }
-    if (lane == 0) bulk_wait_group<0>();
+    if (lane == 0) bulk_wait_group_read<0>();  // smem reads done; the global writes complete with the grid
     __syncwarp();
   }
 

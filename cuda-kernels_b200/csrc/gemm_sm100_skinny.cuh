@@ -32,7 +32,7 @@ struct SkinnyParams {
   int32_t M, N, K;
   int32_t num_k_blk;     // total K-blocks of 64
   int32_t kb_per_split;  // K-blocks per CTA of a cluster
-  int32_t splits;        // S = cluster size along x
+  int32_t splits;        // S = cluster size along x: 1, 2, 4 or 8
   uint64_t timeout_ns;
   uint32_t* status;
 };
@@ -52,12 +52,15 @@ struct SkinnySmemPlan {
   static constexpr int kBytes = kOffAbort + 4;
   static constexpr int kAllocBytes = kBytes + 1024;
   static constexpr int kTmemCols = MPAD <= 32 ? 32 : (MPAD <= 64 ? 64 : (MPAD <= 128 ? 128 : 256));
-  // Epilogue scratch inside the (then idle) ring: partials of the S-1 other
-  // CTAs ([S-1][MPAD][128] fp32) followed by four per-warp bf16 staging
-  // tiles ([MPAD][32] each).
-  static constexpr int kPartialBytes = MPAD * kSkinnyBN * 4;
+  // Epilogue scratch inside the (then idle) ring, for S splits: partials of
+  // the S-1 other CTAs for this CTA's 128/S rows ([S-1][MPAD][128/S] fp32),
+  // then four per-warp bf16 staging tiles ([MPAD][32] each).
   static constexpr int kStagingBytes = MPAD * 32 * 2;
-  static constexpr int max_splits() { return 1 + (kRingBytes - 4 * kStagingBytes) / kPartialBytes; }
+  static constexpr bool fits(int S) {
+    return (S - 1) * MPAD * (kSkinnyBN / S) * 4 + 4 * kStagingBytes <= kRingBytes;
+  }
+  // Largest power-of-two split count (<= 8) whose reduction scratch fits.
+  static constexpr int max_splits() { return fits(8) ? 8 : fits(4) ? 4 : fits(2) ? 2 : 1; }
   static_assert(kAllocBytes <= 232448, "shared memory plan exceeds 227 KiB");
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 256, "UMMA N must be 16..256 in steps of 16");
 };
@@ -223,95 +226,109 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // written; it contributes zero.
   const bool acc_valid = my_kb > 0;
 
-  // Split-K: non-leader CTAs push their fp32 partials into the leader's idle
-  // ring; the leader adds them.  Two cluster barriers: the first guarantees the
-  // leader's ring is no longer read by its MMAs, the second that all partials
-  // have landed.
-  if (p.splits > 1) {
+  // Split-K reduction, distributed: with S = p.splits (1, 2, 4 or 8) CTA r of
+  // the cluster owns tile rows [r*R, (r+1)*R), R = 128 / S, and receives the
+  // other CTAs' partial sums of exactly those rows into its (then idle) ring
+  // over distributed shared memory.  Two cluster barriers: the first
+  // guarantees every ring is no longer read by its MMAs, the second that all
+  // partials have landed.  Every CTA then rounds and stores its own rows.
+  const int S = p.splits;
+  const int R = kSkinnyBN / S;
+  const int row = q * 32 + (int)lane;  // this lane's tile row (TMEM lane)
+  const int owner = row / R;
+  const int row_in_owner = row - owner * R;
+  const uint32_t recv_base = base;     // [S-1 senders][MPAD][R] fp32
+  auto recv_addr = [&](int sender, int owner_rank, int c, int r) {
+    const int slot_ = sender < owner_rank ? sender : sender - 1;
+    return recv_base + (uint32_t)(((slot_ * MPAD + c) * R + r) * 4);
+  };
+  auto tmem_load16 = [&](int c, uint32_t (&v)[16]) {
+    if (acc_valid) {
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          : "r"(tmem_row + (uint32_t)c));
+      asm volatile(
+          "tcgen05.wait::ld.sync.aligned;"
+          : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+            "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+          :
+          : "memory");
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = 0u;
+    }
+  };
+
+  if (S > 1) {
     cluster_sync_all();
-    if (epi && have_acc && rank != 0) {
-      const uint32_t dst0 = mapa_shared(base + (rank - 1u) * Plan::kPartialBytes, 0);
-      const int n_local = q * 32 + (int)lane;
+    if (epi && have_acc) {
+      const bool remote = owner != (int)rank;
+      const uint32_t dst_base = remote ? mapa_shared(recv_addr((int)rank, owner, 0, row_in_owner), (uint32_t)owner) : 0u;
 #pragma unroll 1
       for (int c = 0; c < MPAD; c += 16) {
         uint32_t v[16];
-        if (acc_valid) {
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-              : "r"(tmem_row + (uint32_t)c));
-          asm volatile(
-              "tcgen05.wait::ld.sync.aligned;"
-              : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
-                "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
-              :
-              : "memory");
-        } else {
+        tmem_load16(c, v);  // whole warp (sync.aligned); only rows owned elsewhere are sent
+        if (remote) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0u;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const uint32_t addr = dst0 + (uint32_t)(((c + j) * kSkinnyBN + n_local) * 4);
-          asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(v[j]) : "memory");
+          for (int j = 0; j < 16; ++j) {
+            asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(dst_base + (uint32_t)((c + j) * R * 4)), "r"(v[j])
+                         : "memory");
+          }
         }
       }
     }
     cluster_sync_all();
   }
 
-  if (epi && have_acc && rank == 0) {
-    const uint32_t stage_buf = base + (uint32_t)((p.splits - 1) * Plan::kPartialBytes + slot * Plan::kStagingBytes);
-    const int n_local = q * 32 + (int)lane;
+  // Warps holding rows this CTA owns: add the partials in split order
+  // 0, 1, ..., S-1 (this CTA's own sum at position `rank`), round to bf16,
+  // stage [MPAD rows m][W columns n] and TMA-store C[m, n0 + first .. +W).
+  const int w_first = max(q * 32, (int)rank * R);            // first owned tile row in this warp
+  const int w_end = min(q * 32 + 32, ((int)rank + 1) * R);   // one past the last
+  if (epi && have_acc && w_first < w_end) {
+    const int W = w_end - w_first;  // 16 or 32 columns of C
+    const bool mine = row >= w_first && row < w_end;
+    const uint32_t stage_buf =
+        base + (uint32_t)((S - 1) * MPAD * R * 4) + (uint32_t)(slot * MPAD * 32 * 2);
 #pragma unroll 1
     for (int c = 0; c < MPAD; c += 16) {
       uint32_t v[16];
-      if (acc_valid) {
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-            : "r"(tmem_row + (uint32_t)c));
-        asm volatile(
-            "tcgen05.wait::ld.sync.aligned;"
-            : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
-              "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
-            :
-            : "memory");
-      } else {
+      tmem_load16(c, v);
+      if (mine) {
+        float f[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0u;
-      }
-      float f[16];
+        for (int j = 0; j < 16; ++j) f[j] = 0.0f;
+        for (int sp = 0; sp < S; ++sp) {
+          if (sp == (int)rank) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]);
-      // Partials are added in split order 1, 2, ..., S-1 after this CTA's own
-      // sum, so the result does not depend on timing.
-      for (int r = 1; r < p.splits; ++r) {
-        const uint32_t src = base + (uint32_t)((r - 1) * Plan::kPartialBytes);
+            for (int j = 0; j < 16; ++j) f[j] += __uint_as_float(v[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float x;
+              asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(recv_addr(sp, (int)rank, c + j, row_in_owner)));
+              f[j] += x;
+            }
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          float x;
-          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(src + (uint32_t)(((c + j) * kSkinnyBN + n_local) * 4)));
-          f[j] += x;
+          const __nv_bfloat16 h = __float2bfloat16_rn(f[j]);
+          const uint16_t hb = *reinterpret_cast<const uint16_t*>(&h);
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(stage_buf + (uint32_t)(((c + j) * W + (row - w_first)) * 2)),
+                       "h"(hb)
+                       : "memory");
         }
-      }
-      // Staging tile of this warp: [MPAD rows m][32 columns n] bf16, row pitch 64 B.
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const __nv_bfloat16 h = __float2bfloat16_rn(f[j]);
-        const uint16_t bits = *reinterpret_cast<const uint16_t*>(&h);
-        asm volatile("st.shared.b16 [%0], %1;" ::"r"(stage_buf + (uint32_t)((c + j) * 64 + lane * 2)), "h"(bits)
-                     : "memory");
       }
     }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(&tmC, stage_buf, n0 + q * 32, 0);  // rows m >= M are clipped by TMA
+      tma_store_2d(&tmC, stage_buf, n0 + w_first, 0);  // box {W, MPAD}; rows m >= M are clipped by TMA
       bulk_commit_group();
-      bulk_wait_group<0>();
+      bulk_wait_group_read<0>();  // smem read done; the global writes complete with the grid
     }
     __syncwarp();
   }
