@@ -415,7 +415,9 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layout", default="kn", choices=["kn", "nk"])
     ap.add_argument("--e2e-steps", type=int, default=30)
-    ap.add_argument("--cublas-steps", type=int, default=500, help="cuBLAS comparison loop length (0: skip)")
+    ap.add_argument("--cublas-steps", type=int, default=-1,
+                    help="cuBLAS comparison loop length (default: same as --steps, so both run under the same "
+                         "power state; 0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-rows", type=int, default=256)
@@ -513,8 +515,8 @@ def main(argv=None) -> int:
 
     # cuBLAS on the same GPU, same rotation (context only; not the product).
     cub_tflops = None
-    if rank == 0 and args.cublas_steps > 0:
-        n_cub = args.cublas_steps
+    if rank == 0 and args.cublas_steps != 0:
+        n_cub = args.steps if args.cublas_steps < 0 else args.cublas_steps
         for i in range(10):
             torch.matmul(A[i % ROTATE], B[i % ROTATE] if layout == "kn" else B[i % ROTATE].t(), out=C[i % ROTATE])
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

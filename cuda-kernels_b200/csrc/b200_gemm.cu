@@ -38,6 +38,11 @@ constexpr int kBN = 256;
 constexpr int kStages = 4;
 constexpr int kPairBN = 256;
 constexpr int kPairStages = 6;
+// Wide pair tiles (256 x 512): each CTA reuses its A rows for 512 output
+// columns, 25 % fewer operand bytes per FLOP than 256 x 256, and 8 MMAs per
+// ring stage.  Used when there is at least one wide tile per CTA pair.
+constexpr int kPairWideBN = 512;
+constexpr int kPairWideStages = 4;
 constexpr int kGroupM = 16;
 
 // Skinny (M <= 128) configurations: UMMA N = MPAD, ring depth per MPAD.
@@ -149,6 +154,7 @@ int init_device(int dev, DeviceState& st) {
     return B200_ERR_CUDA;
   constexpr int single_smem = b200::SmemPlan<kBN, kStages>::kAllocBytes;
   constexpr int pair_smem = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
+  constexpr int wide_smem = b200::PairSmemPlan<kPairWideBN, kPairWideStages>::kAllocBytes;
   if (cudaFuncSetAttribute(b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, single_smem) != cudaSuccess ||
       cudaFuncSetAttribute(b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>,
@@ -156,7 +162,11 @@ int init_device(int dev, DeviceState& st) {
       cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess ||
       cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess)
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem) != cudaSuccess)
     return B200_ERR_CUDA;
   if (set_skinny_attrs<16>() != B200_OK || set_skinny_attrs<32>() != B200_OK || set_skinny_attrs<64>() != B200_OK ||
       set_skinny_attrs<128>() != B200_OK)
@@ -363,8 +373,33 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
   }
   const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM);
-  const uint32_t bn = use_pair ? (uint32_t)kPairBN : (uint32_t)kBN;
-  const uint32_t b_rows = use_pair ? bn / 2 : bn;  // B rows (K-major) one CTA loads per K-block
+  const int64_t m_blk_pair = (M + b200::kPairBM - 1) / b200::kPairBM;
+  const int32_t k_blks = (int32_t)((K + b200::kBK - 1) / b200::kBK);
+  // Split-K tail (only with a caller workspace) runs on 256 x 256 tiles.
+  SplitPlan split{};
+  bool use_split = false;
+  if (use_pair && workspace != nullptr) {
+    split = plan_split(m_blk_pair * ((N + kPairBN - 1) / kPairBN), k_blks, st->max_pairs, kPairBN);
+    use_split = split.parts >= 2 && workspace_bytes >= split.bytes() &&
+                (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) == 0;
+  }
+  // Otherwise 256 x 512 tiles, unless they quantise worse onto the CTA pairs:
+  // useful fraction of the launched waves, counting the unused columns of a
+  // partial last tile.  The wide tile moves 25 % fewer operand bytes per FLOP,
+  // so it may lose up to 3 % here (B200: 8192^3 +5 %, 16384^3 +11 %, but
+  // 5000x4096x4096, 3 waves for 2.16 waves of work, -8 %).
+  auto wave_eff = [&](int64_t bn_) {
+    const int64_t n_blk = (N + bn_ - 1) / bn_;
+    const int64_t t = m_blk_pair * n_blk;
+    const int64_t rounds = (t + st->max_pairs - 1) / st->max_pairs;
+    return ((double)t / (double)(rounds * st->max_pairs)) * ((double)N / (double)(n_blk * bn_));
+  };
+  const bool use_wide = use_pair && !use_split &&
+                        m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= st->max_pairs &&
+                        wave_eff(kPairWideBN) >= 0.97 * wave_eff(kPairBN);
+  const uint32_t bn = !use_pair ? (uint32_t)kBN : use_wide ? (uint32_t)kPairWideBN : (uint32_t)kPairBN;
+  // B rows (K-major) one TMA box covers: a pair CTA loads 128-column blocks.
+  const uint32_t b_rows = use_pair ? 128u : bn;
 
   CUtensorMap tmA, tmB, tmC;
   if ((rc = encode_2d(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, b200::kBK, b200::kBM, true)) != B200_OK)
@@ -418,10 +453,9 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   p.sk_parts = 1;
   p.sk_kpp = p.num_k_blk;
   p.num_work = p.num_tiles;
-  if (workspace != nullptr) {
-    const SplitPlan sp = plan_split(tiles, p.num_k_blk, st->max_pairs, kPairBN);
-    if (sp.parts >= 2 && workspace_bytes >= sp.bytes() &&
-        (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) == 0) {
+  if (use_split) {
+    const SplitPlan& sp = split;
+    {
       p.sk_first = sp.first;
       p.sk_parts = sp.parts;
       p.sk_kpp = sp.kpp;
@@ -448,13 +482,21 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
-  cfg.dynamicSmemBytes = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
+  cfg.dynamicSmemBytes = use_wide ? b200::PairSmemPlan<kPairWideBN, kPairWideStages>::kAllocBytes
+                                  : b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e =
-      p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>, tmA, tmB, tmC, p)
-                   : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>, tmA, tmB, tmC, p);
+  cudaError_t e;
+  if (use_wide) {
+    e = p.b_mn_major
+            ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true>, tmA, tmB, tmC, p)
+            : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false>, tmA, tmB, tmC,
+                                 p);
+  } else {
+    e = p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>, tmA, tmB, tmC, p)
+                     : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>, tmA, tmB, tmC, p);
+  }
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 

@@ -37,21 +37,35 @@ constexpr int kPairBM = 256;  // rows of C per pair tile (128 per CTA)
 
 template <int BN, int STAGES>
 struct PairSmemPlan {
-  static constexpr int kHalfN = BN / 2;
+  // A tile of BN columns is computed as kNSub pair MMAs of N = 256 each
+  // (N = 256 is the UMMA maximum).  For sub-tile h, CTA r holds the B columns
+  // [h*256 + r*128, h*256 + r*128 + 128) of the tile, so TMEM column c of the
+  // accumulator is tile column c.
+  static constexpr int kMmaN = BN < 256 ? BN : 256;
+  static constexpr int kNSub = BN / kMmaN;
+  static constexpr int kSubCols = kMmaN / 2;            // B columns per CTA per sub-tile
+  static constexpr int kHalfN = BN / 2;                  // B columns per CTA
+  // Accumulator buffers in TMEM: two (the epilogue of one tile overlaps the
+  // next tile's MMAs) when they fit, else one whose sub-tiles are released
+  // one by one.
+  static constexpr int kAccN = 2 * BN <= kTmemCols ? 2 : 1;
   static constexpr int kABytes = kBM * kBK * 2;        // this CTA's 128 rows of A: 16 KiB
-  static constexpr int kBBytes = kHalfN * kBK * 2;     // this CTA's half of B: 16 KiB for BN = 256
+  static constexpr int kBSubBytes = kSubCols * kBK * 2;  // one sub-tile's B columns of this CTA
+  static constexpr int kBBytes = kNSub * kBSubBytes;     // 16 KiB (BN = 256) or 32 KiB (BN = 512)
   static constexpr int kStageBytes = kABytes + kBBytes;  // per CTA
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + STAGES * kABytes;
   static constexpr int kOffC = kOffB + STAGES * kBBytes;
   static constexpr int kOffBar = kOffC + kEpiWarps * 2 * kEpiBufBytes;
-  static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1;
+  // barriers: full[STAGES], empty[STAGES], acc_full[kAccN], acc_empty[kAccN][kNSub], drain
+  static constexpr int kNumBars = 2 * STAGES + kAccN + kAccN * kNSub + 1;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAbort = kOffTmemHolder + 4;
   static constexpr int kBytes = kOffAbort + 4;
   static constexpr int kAllocBytes = kBytes + 1024;
   static_assert(kAllocBytes <= 232448, "shared memory plan exceeds 227 KiB");
-  static_assert(kHalfN % 64 == 0, "each CTA's half of the B tile must be whole 64-column swizzle atoms");
+  static_assert(kSubCols % 64 == 0, "each CTA's B columns per sub-tile must be whole 64-column swizzle atoms");
+  static_assert(kAccN * BN <= kTmemCols, "accumulators must fit in TMEM");
 };
 
 template <int BN, int STAGES, bool B_MN>
@@ -62,9 +76,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
 #else
   using Plan = PairSmemPlan<BN, STAGES>;
-  constexpr int kHalfN = Plan::kHalfN;
-  static_assert(BN % kEpiCols == 0 && BN >= 128 && BN <= 256, "BN must be 128..256 in steps of 64");
-  static_assert(kAccBufs * BN <= kTmemCols, "accumulators must fit in TMEM");
+  constexpr int kNSub = Plan::kNSub;
+  constexpr int kAccN = Plan::kAccN;
+  static_assert(BN == 256 || BN == 512, "pair tiles are 256 x 256 or 256 x 512");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -78,8 +92,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
   auto accf_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
-  auto acce_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + kAccBufs + b); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 2 * kAccBufs);
+  auto acce_bar = [&](int b, int h) { return bar0 + 8u * (2 * STAGES + kAccN + b * kNSub + h); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + kAccN + kAccN * kNSub);
   volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
 
@@ -95,9 +109,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(full_bar(s), 1);   // leader's producer arrive + both CTAs' transaction bytes
       mbar_init(empty_bar(s), 1);  // one commit from the leader's MMA thread
     }
-    for (int b = 0; b < kAccBufs; ++b) {
-      mbar_init(accf_bar(b), 1);              // one commit from the leader's MMA thread
-      mbar_init(acce_bar(b), 2 * kEpiWarps);  // (leader's copy) every epilogue warp of the pair
+    for (int b = 0; b < kAccN; ++b) {
+      mbar_init(accf_bar(b), 1);  // one commit from the leader's MMA thread
+      for (int h = 0; h < kNSub; ++h) mbar_init(acce_bar(b, h), 2 * kEpiWarps);  // every epilogue warp of the pair
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0u;
@@ -132,7 +146,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int w = pair; w < p.num_work && ok; w += num_pairs) {
         const WorkItem wk = work_item(w, p);
         const int row0 = wk.mb * kPairBM + (int)rank * kBM;
-        const int col0 = wk.nb * BN + (int)rank * kHalfN;
+        const int col0 = wk.nb * BN + (int)rank * Plan::kSubCols;  // + h * kMmaN for sub-tile h
         for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
             ok = false;
@@ -141,13 +155,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint32_t fb = mapa_shared(full_bar(stage), 0);
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * Plan::kStageBytes);
           tma_load_2d_pair(sA + stage * Plan::kABytes, &tmA, fb, kb * kBK, row0, pol);
-          const uint32_t dstB = sB + stage * Plan::kBBytes;
-          if constexpr (!B_MN) {
-            tma_load_2d_pair(dstB, &tmB, fb, kb * kBK, col0, pol);
-          } else {
 #pragma unroll
-            for (int j = 0; j < kHalfN / 64; ++j) {
-              tma_load_2d_pair(dstB + j * (64 * kBK * 2), &tmB, fb, col0 + 64 * j, kb * kBK, pol);
+          for (int h = 0; h < kNSub; ++h) {
+            const uint32_t dstB = sB + stage * Plan::kBBytes + h * Plan::kBSubBytes;
+            const int colh = col0 + h * Plan::kMmaN;
+            if constexpr (!B_MN) {
+              tma_load_2d_pair(dstB, &tmB, fb, kb * kBK, colh, pol);
+            } else {
+#pragma unroll
+              for (int j = 0; j < Plan::kSubCols / 64; ++j) {
+                tma_load_2d_pair(dstB + j * (64 * kBK * 2), &tmB, fb, colh + 64 * j, kb * kBK, pol);
+              }
             }
           }
           ++issued;
@@ -177,7 +195,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer (leader CTA only) ---------------------------------------------
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kPairBM, BN, false, B_MN);
+      constexpr uint32_t idesc = idesc_bf16_f32(kPairBM, Plan::kMmaN, false, B_MN);
       // Descriptors of stage 0; later stages and K slices only move the
       // start-address field (bits 0..13, address >> 4), which never carries.
       //   A, K-major SW128: 128-byte rows, 8-row groups 1024 B apart; the k-th
@@ -195,12 +213,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       bool ok = true;
       for (int w = pair; w < p.num_work && ok; w += num_pairs) {
         const WorkItem wk = work_item(w, p);
-        if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        // Sub-tile h of this accumulator may be written once the epilogue has
+        // drained it (checked right before its first MMA of the tile).
+        bool free_h[kNSub];
+#pragma unroll
+        for (int h = 0; h < kNSub; ++h) free_h[h] = false;
         for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, abort_flag)) {
             ok = false;
@@ -210,9 +228,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint64_t ad = a_desc0 + (uint64_t)((stage * Plan::kABytes) >> 4);
           const uint64_t bd = b_desc0 + (uint64_t)((stage * Plan::kBBytes) >> 4);
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            umma_bf16_pair(d_tmem, ad + 2u * k, bd + kBStep * k, idesc, (kb != wk.kb0 || k != 0) ? 1u : 0u);
+          for (int h = 0; h < kNSub; ++h) {
+            if (!free_h[h]) {
+              if (!mbar_wait(acce_bar(acc, h), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              free_h[h] = true;
+            }
+            const uint64_t bdh = bd + (uint64_t)((h * Plan::kBSubBytes) >> 4);
+#pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              umma_bf16_pair(d_tmem + (uint32_t)(h * Plan::kMmaN), ad + 2u * k, bdh + kBStep * k, idesc,
+                             (kb != wk.kb0 || k != 0) ? 1u : 0u);
+            }
           }
+          if (!ok) break;
           // Stage `stage` is free in both CTAs once these MMAs have read it.
           umma_commit_pair_both(empty_bar(stage));
           if (++stage == STAGES) {
@@ -222,7 +254,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         if (!ok) break;
         umma_commit_pair_both(accf_bar(acc));  // accumulator ready for both CTAs' epilogues
-        if (++acc == kAccBufs) {
+        if (++acc == kAccN) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -276,10 +308,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, r1);
         tmem_ld_wait_regs(r0);
         tmem_ld_wait_regs(r1);
-        if (c == BN / kEpiCols - 1) {
+        if (((c + 1) * kEpiCols) % Plan::kMmaN == 0) {
+          // Sub-tile (c * 64) / 256 of this accumulator is drained: hand it back.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(acce_bar(acc), 0));
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(acce_bar(acc, (c * kEpiCols) / Plan::kMmaN), 0));
         }
         if (sk_writer) {
           // fp32 partial, layout [BN/4][128 rows][4]: a warp's 32 rows of one
@@ -340,7 +373,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         named_bar_sync(1, kEpiWarps * 32);
         if (warp == 2 && lane == 0) st_release_gpu(p.flags + slot_index(wk.part), p.epoch);
       }
-      if (++acc == kAccBufs) {
+      if (++acc == kAccN) {
         acc = 0;
         acc_phase ^= 1u;
       }

@@ -84,7 +84,8 @@ def _rows(M, n, seed):
 
 
 @pytest.mark.parametrize("layout", ["nk", "kn"])
-@pytest.mark.parametrize("shape", [(2048, 4096, 128), (4096, 4096, 64), (1024, 1024, 8192), (640, 2560, 520)],
+@pytest.mark.parametrize("shape", [(2048, 4096, 128), (4096, 4096, 64), (1024, 1024, 8192), (640, 2560, 520),
+                                   (4100, 4000, 200), (4096, 4136, 72)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_persistent_multi_tile_vs_oracle(shape, layout):
     """More tiles than SMs (each CTA loops over several tiles, both TMEM
