@@ -16,7 +16,8 @@ operands in L2.  Clocks are sampled through NVML during the timed region.
 
 `e2e` repeats the step through the public API with host (pinned) buffers:
 host->device copy of the step's A (and of B by rank 0, then NCCL broadcast),
-the GEMM, and the device->host copy of C, all inside the timed region.
+the GEMM, and the device->host copy of C, all inside the timed region,
+pipelined over three streams as a serving loop would run it.
 
 `--impl reference` times the reference's arithmetic on the host cores (the
 reference has no CPU implementation of its own; this is the oracle port in
@@ -132,7 +133,7 @@ def _dist_setup():
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
@@ -358,25 +359,36 @@ def run_rowshard(args) -> int:
     def step(bcast):
         row_sharded_gemm(a, b, M=M, b_layout="nk", chunks=args.chunks, out=c, broadcast=bcast)
 
+    # Warm up to the power-capped steady state (>= 1.5 s of GEMMs) and time at
+    # least ~1 s, so every N is measured in the same clock regime.
     res = {}
     for name, bcast in (("gemm_only", False), ("broadcast_plus_gemm", world > 1)):
-        for _ in range(max(args.warmup, 3)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step(bcast)
+        e1.record()
+        torch.cuda.synchronize()
+        # All ranks must issue the same number of collectives: agree on the
+        # step time (max over ranks) before deriving the step counts from it.
+        one = max(_max_over_ranks(e0.elapsed_time(e1), world), 1e-3)
+        warm = max(args.warmup, int(1500.0 / one) + 1)
+        steps = max(args.steps, int(1000.0 / one) + 1)
+        for _ in range(warm):
             step(bcast)
         torch.cuda.synchronize()
         _barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             step(bcast)
         e1.record()
         torch.cuda.synchronize()
         _barrier(world)
-        res[name] = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+        res[name] = _max_over_ranks(e0.elapsed_time(e1) / steps, world)
     b200_gemm.check_status()
     flops = 2.0 * M * N * K
     if rank == 0:
         print(json.dumps({
-            "metric": "bf16_gemm_tflops_rowshard_131072x8192x8192", "n_gpus": world, "steps": args.steps,
+            "metric": "bf16_gemm_tflops_rowshard_131072x8192x8192", "n_gpus": world, "steps": steps,
             "value": round(flops / (res["broadcast_plus_gemm"] / 1e3) / 1e12, 2), "unit": "TFLOPS",
             "ms_per_step": round(res["broadcast_plus_gemm"], 4), "gemm_only_ms": round(res["gemm_only"], 4),
             "gemm_only_tflops": round(flops / (res["gemm_only"] / 1e3) / 1e12, 2), "scaling": "strong",
@@ -578,7 +590,12 @@ def main(argv=None) -> int:
 
 
 def _e2e(args, world, rank, dev, layout, b200_gemm):
-    """Host buffers -> device -> GEMM -> host, every step, through the public API."""
+    """Host buffers -> device -> GEMM -> host, every step, through the public API.
+
+    Pipelined like a serving loop: three streams (copy in, compute, copy out)
+    and two device buffer sets, so step i+1's host->device copy and step i-1's
+    device->host copy overlap step i's GEMM.  Every step still moves its own
+    inputs in and its result out inside the timed region."""
     import torch
     import torch.distributed as dist
     M, N, K = M_PER_RANK, N_DIM, K_DIM
@@ -586,38 +603,61 @@ def _e2e(args, world, rank, dev, layout, b200_gemm):
     g = torch.Generator().manual_seed(99 + rank)
     a_h = ((torch.rand((M, K), generator=g) * 2 - 1).to(torch.bfloat16)).pin_memory()
     b_h = ((torch.rand(b_shape, generator=g) * 2 - 1).to(torch.bfloat16)).pin_memory() if rank == 0 else None
-    c_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    a_d = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
-    b_d = torch.empty(b_shape, dtype=torch.bfloat16, device=dev)
-    c_d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    c_h = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    a_d = [torch.empty((M, K), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    b_d = [torch.empty(b_shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    c_d = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_comp + ev_out:
+        e.record(torch.cuda.current_stream(dev))
 
-    def step():
-        if rank == 0:
-            b_d.copy_(b_h, non_blocking=True)
-        if world > 1:
-            dist.broadcast(b_d, src=0)
-        a_d.copy_(a_h, non_blocking=True)
-        b200_gemm.gemm(a_d, b_d, b_layout=layout, out=c_d)
-        c_h.copy_(c_d, non_blocking=True)
+    def step(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_comp[j])  # the GEMM that last read a_d[j]/b_d[j] is done
+            if rank == 0:
+                b_d[j].copy_(b_h, non_blocking=True)
+            if world > 1:
+                dist.broadcast(b_d[j], src=0)
+            a_d[j].copy_(a_h, non_blocking=True)
+            ev_in[j].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_in[j])
+            s_comp.wait_event(ev_out[j])  # c_d[j] has been copied out
+            b200_gemm.gemm(a_d[j], b_d[j], b_layout=layout, out=c_d[j])
+            ev_comp[j].record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_comp[j])
+            c_h[j].copy_(c_d[j], non_blocking=True)
+            ev_out[j].record(s_out)
 
-    for _ in range(3):
-        step()
+    for i in range(3):
+        step(i)
     torch.cuda.synchronize()
     _barrier(world)
+    main = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.e2e_steps):
-        step()
-    e1.record()
+    e0.record(main)
+    for s_ in (s_in, s_comp, s_out):
+        s_.wait_stream(main)
+    for i in range(args.e2e_steps):
+        step(i)
+    for s_ in (s_in, s_comp, s_out):
+        main.wait_stream(s_)
+    e1.record(main)
     torch.cuda.synchronize()
     _barrier(world)
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
     tflops = world * FLOPS_PER_STEP * args.e2e_steps / (ms / 1e3) / 1e12
     h2d = a_h.numel() * 2 + (b_h.numel() * 2 if rank == 0 else 0)
     return {"value": round(tflops, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": c_h.numel() * 2, "steps": args.e2e_steps,
+            "d2h_bytes_per_step": c_h[0].numel() * 2, "steps": args.e2e_steps,
             "ms_per_step": round(ms / args.e2e_steps, 4),
-            "path": "pinned host A,B -> H2D -> b200_gemm.gemm (C ABI) -> D2H C, one stream"
+            "path": "pinned host A,B -> H2D -> b200_gemm.gemm (C ABI) -> D2H C every step; copy-in, GEMM and "
+                    "copy-out on three streams with two buffer sets (step i+1 in, i compute, i-1 out overlap)"
                     + ("; B from rank 0 via NCCL broadcast" if world > 1 else "")}
 
 
