@@ -340,9 +340,10 @@ def run_sweep(args) -> int:
 
 def run_rowshard(args) -> int:
     """--rowshard: BASELINE config 5, M=131072, N=K=8192 split into row panels
-    over the ranks (strong scaling).  Each step: B broadcast from rank 0 over
-    NCCL (in N-chunks overlapped with the GEMM, B stored [N,K]) + the GEMM of
-    every panel; device time, max over ranks.  Also reports the GEMM alone."""
+    over the ranks (strong scaling).  Each step: B (stored [N,K]) broadcast
+    from rank 0 over NCCL, whole or in --chunks column chunks overlapped with
+    the GEMM, + the GEMM of every panel; device time, max over ranks.  Also
+    reports the GEMM alone and the optional C all-gather, timed separately."""
     import torch
     import torch.distributed as dist
     world, rank, local = _dist_setup()
@@ -385,6 +386,24 @@ def run_rowshard(args) -> int:
         _barrier(world)
         res[name] = _max_over_ranks(e0.elapsed_time(e1) / steps, world)
     b200_gemm.check_status()
+    # Optional C all-gather (every rank ends with the whole [M, N] C), timed
+    # separately as the BASELINE asks.
+    gather_ms = None
+    if world > 1:
+        from b200_gemm.dist import gather_rows
+        full = gather_rows(c, M)
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            full = gather_rows(c, M)
+        e1.record()
+        torch.cuda.synchronize()
+        _barrier(world)
+        gather_ms = _max_over_ranks(e0.elapsed_time(e1) / reps, world)
+        del full
     flops = 2.0 * M * N * K
     if rank == 0:
         print(json.dumps({
@@ -392,6 +411,7 @@ def run_rowshard(args) -> int:
             "value": round(flops / (res["broadcast_plus_gemm"] / 1e3) / 1e12, 2), "unit": "TFLOPS",
             "ms_per_step": round(res["broadcast_plus_gemm"], 4), "gemm_only_ms": round(res["gemm_only"], 4),
             "gemm_only_tflops": round(flops / (res["gemm_only"] / 1e3) / 1e12, 2), "scaling": "strong",
+            "c_allgather_ms": round(gather_ms, 3) if gather_ms is not None else None,
             "config": {"M": M, "N": N, "K": K, "b_layout": "nk", "chunks": args.chunks,
                        "panel_rows": e - s, "timing": "device, max over ranks"}}), flush=True)
     if world > 1:
@@ -441,7 +461,7 @@ def main(argv=None) -> int:
     ap.add_argument("--target-ms", type=float, default=250.0)
     ap.add_argument("--rowshard", action="store_true", help="BASELINE config 5: row-sharded 131072x8192x8192")
     ap.add_argument("--rowshard-m", type=int, default=131072)
-    ap.add_argument("--chunks", type=int, default=4)
+    ap.add_argument("--chunks", type=int, default=1, help="--rowshard: column chunks of B broadcast one by one")
     args = ap.parse_args(argv)
     if args.rowshard:
         return run_rowshard(args)

@@ -14,6 +14,13 @@ single-GPU kernel collection); this driver is new.  Design points:
     on the compute stream as soon as chunk j has arrived (CUDA event), so
     the broadcast overlaps the GEMM of the chunks before it.  [K,N] B is
     broadcast whole (its column chunks are not contiguous).
+  * The persistent GEMM occupies every SM, so an NCCL kernel queued behind
+    it starts only between two GEMM launches.  On B200 (NVLink 5, NVSwitch)
+    one whole-B broadcast before the GEMM measured fastest at 4 and 8 GPUs
+    (128 MiB at ~560 GB/s, 0.24 ms): chunking adds a serialised broadcast
+    per chunk, and leaving SMs free for the broadcast (GEMM grid limited,
+    NCCL limited to as many CTAs) cost the GEMM more than it hid.  `chunks`
+    stays available; 1 is the default.
   * No kernel reads another GPU's memory: B lands in each GPU's own HBM
     first.
   * The GEMM is pluggable (`gemm_fn`) so the host logic can be tested with
@@ -74,7 +81,7 @@ def broadcast_b(b: torch.Tensor, src: int = 0, group=None) -> None:
 
 
 def row_sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, *, M: int, b_layout: str = "kn", src: int = 0,
-                     group=None, chunks: int = 4, out: torch.Tensor | None = None,
+                     group=None, chunks: int = 1, out: torch.Tensor | None = None,
                      gemm_fn: GemmFn | None = None, broadcast: bool = True) -> ShardedResult:
     """One row-sharded GEMM step on this rank.
 
@@ -83,6 +90,8 @@ def row_sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, *, M: int, b_layout
               shape and dtype that receives it (unless broadcast=False, in
               which case every rank already holds B)
     M       : global number of rows of A (used to check the panel size)
+    chunks  : number of column chunks of an [N,K] B to broadcast and
+              multiply one after another (1 = whole B, then the GEMM)
     """
     gemm_fn = gemm_fn or _default_gemm
     world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -112,7 +121,7 @@ def row_sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, *, M: int, b_layout
     bounds = chunk_bounds(N, chunks)
     if use_streams:
         compute = torch.cuda.current_stream(a_local.device)
-        comm = torch.cuda.Stream(device=a_local.device)
+        comm = _comm_stream(a_local.device)
         comm.wait_stream(compute)
         events = []
         with torch.cuda.stream(comm):
@@ -130,6 +139,17 @@ def row_sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, *, M: int, b_layout
             dist.broadcast(b[s:e], src=src, group=group)
             gemm_fn(a_local, b[s:e], b_layout="nk", out=out[:, s:e])
     return ShardedResult(out, start, stop)
+
+
+_COMM_STREAMS: dict = {}
+
+
+def _comm_stream(device) -> "torch.cuda.Stream":
+    """One side stream per device for the broadcasts (reused across calls)."""
+    key = torch.device(device).index
+    if key not in _COMM_STREAMS:
+        _COMM_STREAMS[key] = torch.cuda.Stream(device=device)
+    return _COMM_STREAMS[key]
 
 
 def gather_rows(c_local: torch.Tensor, M: int, group=None) -> torch.Tensor:

@@ -84,6 +84,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.T
         # stream-safe, so concurrent calls never share a workspace.
         ws_bytes = workspace_bytes(M, N, K, b_layout) if split_k else 0
         ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=a.device) if ws_bytes else None
+        if ws is not None and stream is not None:
+            ws.record_stream(s)  # allocated on the current stream, used on `s`
         ws_ptr = ((ws.data_ptr() + 255) // 256 * 256) if ws is not None else None
         rc = lib.b200_gemm_bf16_ws(
             ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()),
@@ -146,3 +148,4 @@ def set_kernel(which: str) -> None:
     rc = _lib.load().b200_gemm_set_kernel(_KERNELS[which])
     if rc != _lib.B200_OK:
         raise B200GemmError(rc)
+

@@ -289,8 +289,6 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   p.num_k_blk = (int32_t)((K + b200::kBK - 1) / b200::kBK);
   const int64_t n_tiles = (N + b200::kSkinnyBN - 1) / b200::kSkinnyBN;
   if (n_tiles > 65535) return B200_ERR_TOO_LARGE;  // grid.y limit
-  // Split K so that (tiles x splits) CTAs cover the SMs once, within the
-  // cluster-size and shared-memory limits; no split is left without K-blocks.
   // Split K so that tiles x splits CTAs cover the SMs once; the split count
   // is a power of two (each CTA of a cluster owns 128/S rows of the
   // reduction), at most 8 (portable cluster size) and at most what the
@@ -373,13 +371,14 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
   }
   const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM);
+  const int max_pairs = st->max_pairs;
   const int64_t m_blk_pair = (M + b200::kPairBM - 1) / b200::kPairBM;
   const int32_t k_blks = (int32_t)((K + b200::kBK - 1) / b200::kBK);
   // Split-K tail (only with a caller workspace) runs on 256 x 256 tiles.
   SplitPlan split{};
   bool use_split = false;
   if (use_pair && workspace != nullptr) {
-    split = plan_split(m_blk_pair * ((N + kPairBN - 1) / kPairBN), k_blks, st->max_pairs, kPairBN);
+    split = plan_split(m_blk_pair * ((N + kPairBN - 1) / kPairBN), k_blks, max_pairs, kPairBN);
     use_split = split.parts >= 2 && workspace_bytes >= split.bytes() &&
                 (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) == 0;
   }
@@ -391,11 +390,11 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   auto wave_eff = [&](int64_t bn_) {
     const int64_t n_blk = (N + bn_ - 1) / bn_;
     const int64_t t = m_blk_pair * n_blk;
-    const int64_t rounds = (t + st->max_pairs - 1) / st->max_pairs;
-    return ((double)t / (double)(rounds * st->max_pairs)) * ((double)N / (double)(n_blk * bn_));
+    const int64_t rounds = (t + max_pairs - 1) / max_pairs;
+    return ((double)t / (double)(rounds * max_pairs)) * ((double)N / (double)(n_blk * bn_));
   };
   const bool use_wide = use_pair && !use_split &&
-                        m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= st->max_pairs &&
+                        m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= max_pairs &&
                         wave_eff(kPairWideBN) >= 0.97 * wave_eff(kPairBN);
   const uint32_t bn = !use_pair ? (uint32_t)kBN : use_wide ? (uint32_t)kPairWideBN : (uint32_t)kPairBN;
   // B rows (K-major) one TMA box covers: a pair CTA loads 128-column blocks.
@@ -471,7 +470,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     }
   }
   const int64_t work = p.num_work;
-  const int pairs = (int)(work < st->max_pairs ? work : st->max_pairs);
+  const int pairs = (int)(work < max_pairs ? work : max_pairs);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -134,7 +134,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
     if (lane == 0) {
-      const uint64_t pol_stream = l2_policy_evict_normal();
+      // Weights are read once: evict them first.  The activation tile is read
+      // by the CTAs of every tile: keep it.
+      const uint64_t pol_b = l2_policy_evict_first();
+      const uint64_t pol_a = l2_policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0;
@@ -148,12 +151,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         mbar_arrive_expect_tx(fb, Plan::kStageBytes);
         const uint32_t dBt = sBt + stage * Plan::kBtBytes;
         if constexpr (!B_MN) {
-          tma_load_2d(dBt, &tmB, fb, kb * kBK, n0, pol_stream);
+          tma_load_2d(dBt, &tmB, fb, kb * kBK, n0, pol_b);
         } else {
-          tma_load_2d(dBt, &tmB, fb, n0, kb * kBK, pol_stream);
-          tma_load_2d(dBt + 64 * kBK * 2, &tmB, fb, n0 + 64, kb * kBK, pol_stream);
+          tma_load_2d(dBt, &tmB, fb, n0, kb * kBK, pol_b);
+          tma_load_2d(dBt + 64 * kBK * 2, &tmB, fb, n0 + 64, kb * kBK, pol_b);
         }
-        tma_load_2d(sAt + stage * Plan::kAtBytes, &tmA, fb, kb * kBK, 0, pol_stream);
+        tma_load_2d(sAt + stage * Plan::kAtBytes, &tmA, fb, kb * kBK, 0, pol_a);
         ++issued;
         if (++stage == STAGES) {
           stage = 0;
