@@ -302,8 +302,9 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   while (splits * 2 <= cap) splits *= 2;
   p.kb_per_split = (int32_t)((p.num_k_blk + splits - 1) / splits);
   p.splits = (int32_t)splits;
-  // Each owner CTA stores a [MPAD x min(32, 128/S)] block of C.
-  const uint32_t box_n = (uint32_t)(b200::kSkinnyBN / splits < 32 ? b200::kSkinnyBN / splits : 32);
+  // C store box: each warp stores [MPAD x 32] without a split; with S splits
+  // each CTA stores its owned rows as one [MPAD x 128/S] block.
+  const uint32_t box_n = (uint32_t)(splits == 1 ? 32 : b200::kSkinnyBN / splits);
   if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, box_n, MPAD, false, false)) != B200_OK)
     return rc;
   p.timeout_ns = st.timeout_ns;

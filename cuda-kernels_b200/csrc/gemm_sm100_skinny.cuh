@@ -9,8 +9,10 @@
 //     operand (always K-major).
 //   * Split-K inside a thread-block cluster: the S CTAs of a cluster share one
 //     128-row tile of N and each takes a contiguous range of K-blocks, so
-//     S x (N / 128) CTAs stream B concurrently.  Partial fp32 tiles are summed
-//     in the leader CTA through distributed shared memory — no global scratch.
+//     S x (N / 128) CTAs stream B concurrently.  The fp32 partial tiles are
+//     reduced through distributed shared memory — no global scratch: CTA r
+//     owns tile rows [r*R, (r+1)*R), R = 128 / S, and every other CTA sends it
+//     their partials of those rows as one bulk shared-to-shared copy.
 //   * Each CTA: warp 0 TMA producer (deep ring of plain loads), warp 1 TMEM
 //     allocation + single-thread tcgen05.mma issue, warps 2..5 epilogue
 //     (TMEM -> registers -> [cluster reduction] -> bf16 -> smem -> TMA store of
@@ -46,21 +48,35 @@ struct SkinnySmemPlan {
   static constexpr int kOffAt = STAGES * kBtBytes;
   static constexpr int kRingBytes = STAGES * kStageBytes;
   static constexpr int kOffBar = kRingBytes;
-  static constexpr int kNumBars = 2 * STAGES + 2;  // full, empty, acc_full, drain
+  static constexpr int kNumBars = 2 * STAGES + 3;  // full, empty, acc_full, drain, reduction
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAbort = kOffTmemHolder + 4;
   static constexpr int kBytes = kOffAbort + 4;
   static constexpr int kAllocBytes = kBytes + 1024;
   static constexpr int kTmemCols = MPAD <= 32 ? 32 : (MPAD <= 64 ? 64 : (MPAD <= 128 ? 128 : 256));
-  // Epilogue scratch inside the (then idle) ring, for S splits: partials of
-  // the S-1 other CTAs for this CTA's 128/S rows ([S-1][MPAD][128/S] fp32),
-  // then four per-warp bf16 staging tiles ([MPAD][32] each).
-  static constexpr int kStagingBytes = MPAD * 32 * 2;
-  static constexpr bool fits(int S) {
-    return (S - 1) * MPAD * (kSkinnyBN / S) * 4 + 4 * kStagingBytes <= kRingBytes;
+  // Epilogue scratch inside the (then idle) ring.  S > 1, R = 128 / S rows
+  // owned per CTA, rows padded to kPitch floats (a lane moves its row with
+  // 16-byte accesses; the odd number of 16-byte units per row spreads
+  // consecutive rows over all banks):
+  //   [0, recv)          the owned rows' partials, one block per split
+  //                      ([S][R][kPitch] fp32; this CTA's own block is
+  //                      staged locally, the others arrive by bulk copy);
+  //   [recv, cstage)     this CTA's partials of the rows the others own
+  //                      ([S-1][R][kPitch] fp32), one bulk copy per owner;
+  //   [cstage, ...)      the bf16 C block of the owned rows, [MPAD][R].
+  // S == 1: four per-warp bf16 C tiles [MPAD][32] at the start of the ring.
+  static constexpr int kPitch = MPAD + 4;
+  __host__ __device__ static constexpr int block_bytes(int S) { return (kSkinnyBN / S) * kPitch * 4; }
+  __host__ __device__ static constexpr int recv_bytes(int S) { return S * block_bytes(S); }
+  __host__ __device__ static constexpr int cstage_off(int S) {
+    return S > 1 ? (recv_bytes(S) + (S - 1) * block_bytes(S) + 1023) & ~1023 : 0;
   }
+  __host__ __device__ static constexpr int cstage_bytes(int S) {
+    return S > 1 ? MPAD * (kSkinnyBN / S) * 2 : 4 * MPAD * 32 * 2;
+  }
+  __host__ __device__ static constexpr bool fits(int S) { return cstage_off(S) + cstage_bytes(S) <= kRingBytes; }
   // Largest power-of-two split count (<= 8) whose reduction scratch fits.
-  static constexpr int max_splits() { return fits(8) ? 8 : fits(4) ? 4 : fits(2) ? 2 : 1; }
+  __host__ __device__ static constexpr int max_splits() { return fits(8) ? 8 : fits(4) ? 4 : fits(2) ? 2 : 1; }
   static_assert(kAllocBytes <= 232448, "shared memory plan exceeds 227 KiB");
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 256, "UMMA N must be 16..256 in steps of 16");
 };
@@ -92,6 +108,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
   const uint32_t accf_bar = bar0 + 8u * (2 * STAGES);
   const uint32_t drain_bar = accf_bar + 8u;
+  const uint32_t red_bar = drain_bar + 8u;  // partials from the other CTAs have landed
   volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
 
@@ -110,6 +127,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     mbar_init(accf_bar, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(red_bar, 1);
+    // Every other CTA of the cluster sends this CTA one block of partials.
+    if (p.splits > 1) mbar_arrive_expect_tx(red_bar, (uint32_t)((p.splits - 1) * Plan::block_bytes(p.splits)));
     *abort_flag = 0u;
     fence_mbar_init();
     tma_prefetch_desc(&tmB);
@@ -214,10 +234,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // ---- epilogue ---------------------------------------------------------------
   // Warps 2..5 read TMEM lanes q*32 .. q*32+31, i.e. N rows n0 + q*32 + lane,
   // all MPAD columns (= rows m of C).
+  constexpr int kChunk = MPAD >= 32 ? 32 : 16;  // TMEM columns per load + wait
   const bool epi = warp >= 2;
   const int q = warp & 3;
   const int slot = warp - 2;
   const uint32_t tmem_row = tmem_base + ((uint32_t)(q * 32) << 16);
+  const int row = q * 32 + (int)lane;  // this lane's tile row (TMEM lane)
+  // my_kb == 0 (more splits than K-blocks): this CTA's accumulator was never
+  // written; it contributes zero.
+  const bool acc_valid = my_kb > 0;
+  auto tmem_chunk = [&](int c, uint32_t (&v)[kChunk]) {
+    if (acc_valid) {
+      if constexpr (kChunk == 32) {
+        tmem_ld_32x32b_x32(tmem_row + (uint32_t)c, v);
+      } else {
+        tmem_ld_32x32b_x16(tmem_row + (uint32_t)c, v);
+      }
+      tmem_ld_wait_regs(v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) v[j] = 0u;
+    }
+  };
   bool have_acc = false;
   if (epi) {
     const bool got = mbar_wait(accf_bar, 0u, p.timeout_ns, abort_flag);
@@ -225,123 +263,147 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (!have_acc && lane == 0) skinny_raise(p, abort_flag, kDevTimeoutEpilogue);
     tc_fence_after();
   }
-  // my_kb == 0 (more splits than K-blocks): this CTA's accumulator was never
-  // written; it contributes zero.
-  const bool acc_valid = my_kb > 0;
-
-  // Split-K reduction, distributed: with S = p.splits (1, 2, 4 or 8) CTA r of
-  // the cluster owns tile rows [r*R, (r+1)*R), R = 128 / S, and receives the
-  // other CTAs' partial sums of exactly those rows into its (then idle) ring
-  // over distributed shared memory.  Two cluster barriers: the first
-  // guarantees every ring is no longer read by its MMAs, the second that all
-  // partials have landed.  Every CTA then rounds and stores its own rows.
   const int S = p.splits;
-  const int R = kSkinnyBN / S;
-  const int row = q * 32 + (int)lane;  // this lane's tile row (TMEM lane)
-  const int owner = row / R;
-  const int row_in_owner = row - owner * R;
-  const uint32_t recv_base = base;     // [S-1 senders][MPAD][R] fp32
-  auto recv_addr = [&](int sender, int owner_rank, int c, int r) {
-    const int slot_ = sender < owner_rank ? sender : sender - 1;
-    return recv_base + (uint32_t)(((slot_ * MPAD + c) * R + r) * 4);
-  };
-  auto tmem_load16 = [&](int c, uint32_t (&v)[16]) {
-    if (acc_valid) {
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-          : "r"(tmem_row + (uint32_t)c));
-      asm volatile(
-          "tcgen05.wait::ld.sync.aligned;"
-          : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
-            "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
-          :
-          : "memory");
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = 0u;
-    }
-  };
 
-  if (S > 1) {
-    cluster_sync_all();
+  if (S == 1) {
+    // Whole tile here: each warp rounds its 32 rows and stores them as one
+    // [MPAD x 32] block of C.
     if (epi && have_acc) {
-      const bool remote = owner != (int)rank;
-      const uint32_t dst_base = remote ? mapa_shared(recv_addr((int)rank, owner, 0, row_in_owner), (uint32_t)owner) : 0u;
+      const uint32_t stage_buf = base + (uint32_t)(slot * MPAD * 32 * 2);
 #pragma unroll 1
-      for (int c = 0; c < MPAD; c += 16) {
-        uint32_t v[16];
-        tmem_load16(c, v);  // whole warp (sync.aligned); only rows owned elsewhere are sent
-        if (remote) {
+      for (int c = 0; c < MPAD; c += kChunk) {
+        uint32_t v[kChunk];
+        tmem_chunk(c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(dst_base + (uint32_t)((c + j) * R * 4)), "r"(v[j])
-                         : "memory");
-          }
+        for (int j = 0; j < kChunk; ++j) {
+          const __nv_bfloat16 hv = __float2bfloat16_rn(__uint_as_float(v[j]));
+          const uint16_t hb = *reinterpret_cast<const uint16_t*>(&hv);
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(stage_buf + (uint32_t)(((c + j) * 32 + (int)lane) * 2)),
+                       "h"(hb)
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmC, stage_buf, n0 + q * 32, 0);  // box {32, MPAD}; rows m >= M, columns >= N clipped
+        bulk_commit_group();
+        bulk_wait_group_read<0>();  // smem read done; the global writes complete with the grid
+      }
+      __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, Plan::kTmemCols);
+    }
+    return;
+  }
+
+  // Split-K reduction, S = 2, 4 or 8.  Two split cluster barriers:
+  //   #1 every CTA's ring is idle (all its MMAs done), so partials may be
+  //      copied into it.  Each CTA arrives as soon as its own MMAs are done
+  //      and stages its partials locally before waiting.
+  //   #2 every copy into every CTA has landed, so no CTA leaves while its
+  //      shared memory is still a copy's source or destination.  Each CTA
+  //      arrives once its incoming blocks are in and rounds, stores its rows
+  //      before waiting.
+  const int R = kSkinnyBN / S;
+  const uint32_t blk = (uint32_t)Plan::block_bytes(S);
+  const uint32_t recv_base = base;                                   // [S][R][kPitch]
+  const uint32_t send_base = base + (uint32_t)Plan::recv_bytes(S);   // [S-1][R][kPitch]
+  const uint32_t cstage = base + (uint32_t)Plan::cstage_off(S);      // bf16 [MPAD][R]
+  cluster_arrive();  // #1: producer and MMA warps are past their drains here
+  bool staged = false;
+  if (epi) {
+    if (have_acc) {
+      const int owner = row / R;
+      const int r_in = row - owner * R;
+      const uint32_t dst_blk = owner == (int)rank ? recv_base + (uint32_t)rank * blk
+                                                  : send_base + (uint32_t)(owner < (int)rank ? owner : owner - 1) * blk;
+      const uint32_t dst_row = dst_blk + (uint32_t)(r_in * Plan::kPitch * 4);
+#pragma unroll 1
+      for (int c = 0; c < MPAD; c += kChunk) {
+        uint32_t v[kChunk];
+        tmem_chunk(c, v);
+#pragma unroll
+        for (int j = 0; j < kChunk; j += 4) {
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst_row + (uint32_t)((c + j) * 4)),
+                       "r"(v[j]), "r"(v[j + 1]), "r"(v[j + 2]), "r"(v[j + 3])
+                       : "memory");
         }
       }
     }
-    cluster_sync_all();
+    fence_proxy_async_smem();  // staged partials -> visible to the bulk copies
+    tc_fence_before();         // TMEM reads of this CTA are done before teardown
+    staged = named_bar_and(1, kEpiWarps * 32, have_acc);
   }
-
-  // Warps holding rows this CTA owns: add the partials in split order
-  // 0, 1, ..., S-1 (this CTA's own sum at position `rank`), round to bf16,
-  // stage [MPAD rows m][W columns n] and TMA-store C[m, n0 + first .. +W).
-  const int w_first = max(q * 32, (int)rank * R);            // first owned tile row in this warp
-  const int w_end = min(q * 32 + 32, ((int)rank + 1) * R);   // one past the last
-  if (epi && have_acc && w_first < w_end) {
-    const int W = w_end - w_first;  // 16 or 32 columns of C
-    const bool mine = row >= w_first && row < w_end;
-    const uint32_t stage_buf =
-        base + (uint32_t)((S - 1) * MPAD * R * 4) + (uint32_t)(slot * MPAD * 32 * 2);
+  cluster_wait();  // #1
+  if (epi && staged && warp == 2 && (int)lane < S - 1) {
+    const int o = (int)lane < (int)rank ? (int)lane : (int)lane + 1;  // owner this lane sends to
+    bulk_copy_to_cluster(mapa_shared(recv_base + (uint32_t)rank * blk, (uint32_t)o), send_base + lane * blk, blk,
+                         mapa_shared(red_bar, (uint32_t)o));
+  }
+  bool go = false;
+  if (epi) {
+    bool in = false;
+    if (staged) {
+      in = mbar_wait(red_bar, 0u, p.timeout_ns, abort_flag);
+      if (!in) skinny_raise(p, abort_flag, kDevTimeoutEpilogue);
+    }
+    go = named_bar_and(2, kEpiWarps * 32, in);
+  }
+  if (warp == 2 && lane == 0 && !go) {
+    // Error path: still let every incoming block land before this CTA can leave.
+    if (!mbar_wait(red_bar, 0u, p.timeout_ns, nullptr)) skinny_raise(p, abort_flag, kDevTimeoutDrain);
+  }
+  cluster_arrive();  // #2
+  if (epi && go) {
+    // Sum the S partials of the owned rows in split order (deterministic),
+    // round to bf16 and stage C[m, n0 + rank*R + r] as [MPAD][R].  The 128
+    // epilogue threads split the block: thread t takes row t % R and CPT
+    // consecutive columns.
+    constexpr int kMinCpt = 4;
+    const int cpt = max(kMinCpt, MPAD * R / (kEpiWarps * 32));
+    const int groups = MPAD / cpt;
+    const int t = (int)threadIdx.x - 64;
+    if (t < R * groups) {
+      const int r = t % R;
+      const int c0 = (t / R) * cpt;
 #pragma unroll 1
-    for (int c = 0; c < MPAD; c += 16) {
-      uint32_t v[16];
-      tmem_load16(c, v);
-      if (mine) {
-        float f[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) f[j] = 0.0f;
+      for (int c = c0; c < c0 + cpt; c += 4) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 1
         for (int sp = 0; sp < S; ++sp) {
-          if (sp == (int)rank) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) f[j] += __uint_as_float(v[j]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float x;
-              asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(recv_addr(sp, (int)rank, c + j, row_in_owner)));
-              f[j] += x;
-            }
-          }
+          float x0, x1, x2, x3;
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(x0), "=f"(x1), "=f"(x2), "=f"(x3)
+                       : "r"(recv_base + (uint32_t)sp * blk + (uint32_t)((r * Plan::kPitch + c) * 4)));
+          a0 += x0;
+          a1 += x1;
+          a2 += x2;
+          a3 += x3;
         }
+        const float a[4] = {a0, a1, a2, a3};
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const __nv_bfloat16 h = __float2bfloat16_rn(f[j]);
-          const uint16_t hb = *reinterpret_cast<const uint16_t*>(&h);
-          asm volatile("st.shared.b16 [%0], %1;" ::"r"(stage_buf + (uint32_t)(((c + j) * W + (row - w_first)) * 2)),
-                       "h"(hb)
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat16 hv = __float2bfloat16_rn(a[j]);
+          const uint16_t hb = *reinterpret_cast<const uint16_t*>(&hv);
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(cstage + (uint32_t)(((c + j) * R + r) * 2)), "h"(hb)
                        : "memory");
         }
       }
     }
     fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(&tmC, stage_buf, n0 + w_first, 0);  // box {W, MPAD}; rows m >= M are clipped by TMA
+    named_bar_sync(1, kEpiWarps * 32);
+    if (warp == 2 && lane == 0) {
+      tma_store_2d(&tmC, cstage, n0 + (int)rank * R, 0);  // box {R, MPAD}; rows m >= M, columns >= N clipped
       bulk_commit_group();
       bulk_wait_group_read<0>();  // smem read done; the global writes complete with the grid
     }
-    __syncwarp();
   }
-
-  tc_fence_before();
-  if (p.splits > 1) {
-    cluster_sync_all();
-  } else {
-    __syncthreads();
-  }
+  cluster_wait();  // #2
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Plan::kTmemCols);
