@@ -29,6 +29,7 @@
 namespace b200 {
 
 constexpr int kSkinnyBN = 128;  // N rows per tile (UMMA M)
+constexpr int kMaxSplits = 8;   // cluster size limit (portable)
 
 struct SkinnyParams {
   int32_t M, N, K;
@@ -243,17 +244,35 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // my_kb == 0 (more splits than K-blocks): this CTA's accumulator was never
   // written; it contributes zero.
   const bool acc_valid = my_kb > 0;
-  auto tmem_chunk = [&](int c, uint32_t (&v)[kChunk]) {
-    if (acc_valid) {
-      if constexpr (kChunk == 32) {
-        tmem_ld_32x32b_x32(tmem_row + (uint32_t)c, v);
-      } else {
-        tmem_ld_32x32b_x16(tmem_row + (uint32_t)c, v);
-      }
-      tmem_ld_wait_regs(v);
+  // TMEM -> registers, kChunk columns starting at column c; issue only (the
+  // registers are valid after tmem_chunk_wait).  All four rows of a warp's
+  // TMEM lanes move at once (sync.aligned: the whole warp executes these).
+  auto tmem_chunk_issue = [&](int c, uint32_t (&v)[kChunk]) {
+    if constexpr (kChunk == 32) {
+      tmem_ld_32x32b_x32(tmem_row + (uint32_t)c, v);
     } else {
+      tmem_ld_32x32b_x16(tmem_row + (uint32_t)c, v);
+    }
+  };
+  auto tmem_chunk_wait = [&](uint32_t (&v)[kChunk]) {
+    tmem_ld_wait_regs(v);
+    if (!acc_valid) {
 #pragma unroll
       for (int j = 0; j < kChunk; ++j) v[j] = 0u;
+    }
+  };
+  // Runs body(c, v) over the MPAD columns in kChunk pieces, loading the next
+  // piece from TMEM while the body consumes the current one.
+  auto for_each_chunk = [&](auto&& body) {
+    constexpr int kN = MPAD / kChunk;
+    uint32_t v[2][kChunk];
+    tmem_chunk_issue(0, v[0]);
+    tmem_chunk_wait(v[0]);
+#pragma unroll
+    for (int i = 0; i < kN; ++i) {
+      if (i + 1 < kN) tmem_chunk_issue((i + 1) * kChunk, v[(i + 1) & 1]);
+      body(i * kChunk, v[i & 1]);
+      if (i + 1 < kN) tmem_chunk_wait(v[(i + 1) & 1]);
     }
   };
   bool have_acc = false;
@@ -270,10 +289,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // [MPAD x 32] block of C.
     if (epi && have_acc) {
       const uint32_t stage_buf = base + (uint32_t)(slot * MPAD * 32 * 2);
-#pragma unroll 1
-      for (int c = 0; c < MPAD; c += kChunk) {
-        uint32_t v[kChunk];
-        tmem_chunk(c, v);
+      for_each_chunk([&](int c, const uint32_t (&v)[kChunk]) {
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
           const __nv_bfloat16 hv = __float2bfloat16_rn(__uint_as_float(v[j]));
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                        "h"(hb)
                        : "memory");
         }
-      }
+      });
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -323,17 +339,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const uint32_t dst_blk = owner == (int)rank ? recv_base + (uint32_t)rank * blk
                                                   : send_base + (uint32_t)(owner < (int)rank ? owner : owner - 1) * blk;
       const uint32_t dst_row = dst_blk + (uint32_t)(r_in * Plan::kPitch * 4);
-#pragma unroll 1
-      for (int c = 0; c < MPAD; c += kChunk) {
-        uint32_t v[kChunk];
-        tmem_chunk(c, v);
+      for_each_chunk([&](int c, const uint32_t (&v)[kChunk]) {
 #pragma unroll
         for (int j = 0; j < kChunk; j += 4) {
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst_row + (uint32_t)((c + j) * 4)),
                        "r"(v[j]), "r"(v[j + 1]), "r"(v[j + 2]), "r"(v[j + 3])
                        : "memory");
         }
-      }
+      });
     }
     fence_proxy_async_smem();  // staged partials -> visible to the bulk copies
     tc_fence_before();         // TMEM reads of this CTA are done before teardown
@@ -371,21 +384,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (t < R * groups) {
       const int r = t % R;
       const int c0 = (t / R) * cpt;
-#pragma unroll 1
+#pragma unroll 2
       for (int c = c0; c < c0 + cpt; c += 4) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 1
-        for (int sp = 0; sp < S; ++sp) {
-          float x0, x1, x2, x3;
-          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                       : "=f"(x0), "=f"(x1), "=f"(x2), "=f"(x3)
-                       : "r"(recv_base + (uint32_t)sp * blk + (uint32_t)((r * Plan::kPitch + c) * 4)));
-          a0 += x0;
-          a1 += x1;
-          a2 += x2;
-          a3 += x3;
+        // All S loads first (independent), then the sum in split order.
+        float4 x[kMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp) {
+          if (sp < S) {
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(x[sp].x), "=f"(x[sp].y), "=f"(x[sp].z), "=f"(x[sp].w)
+                         : "r"(recv_base + (uint32_t)sp * blk + (uint32_t)((r * Plan::kPitch + c) * 4)));
+          }
         }
-        const float a[4] = {a0, a1, a2, a3};
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp) {
+          if (sp < S) {
+            a[0] += x[sp].x;
+            a[1] += x[sp].y;
+            a[2] += x[sp].z;
+            a[3] += x[sp].w;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const __nv_bfloat16 hv = __float2bfloat16_rn(a[j]);
