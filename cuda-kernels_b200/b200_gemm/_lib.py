@@ -24,10 +24,19 @@ B200_ERR_SCRATCH_LIMIT = 8
 B200_B_NK = 0
 B200_B_KN = 1
 
+B200_DTYPE_BF16 = 0
+B200_DTYPE_F32 = 1
+
 B200_KERNEL_AUTO = 0
 B200_KERNEL_SINGLE = 1
 B200_KERNEL_PAIR = 2
 B200_KERNEL_SKINNY = 3
+
+class Epilogue(ctypes.Structure):
+    """struct b200_epilogue (include/b200_gemm.h)."""
+    _fields_ = [("alpha", ctypes.c_float), ("beta", ctypes.c_float), ("c_in", ctypes.c_void_p),
+                ("ldc_in", ctypes.c_int64), ("bias", ctypes.c_void_p), ("d_dtype", ctypes.c_int)]
+
 
 # Every symbol include/b200_gemm.h declares, with its ctypes signature.
 _SIGNATURES = {
@@ -39,6 +48,10 @@ _SIGNATURES = {
                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "b200_gemm_bf16_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int, ctypes.POINTER(Epilogue), ctypes.c_void_p]),
     "b200_gemm_bf16_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                               ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

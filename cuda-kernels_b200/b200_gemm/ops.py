@@ -39,8 +39,17 @@ def _check_operand(name: str, t: torch.Tensor) -> None:
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.Tensor | None = None,
-         stream: torch.cuda.Stream | None = None, split_k: bool = False) -> torch.Tensor:
+         stream: torch.cuda.Stream | None = None, split_k: bool = False, alpha: float = 1.0, beta: float = 0.0,
+         c: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+         out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     """C = A @ op(B) in bf16 with fp32 accumulation on a B200 (sm_100a).
+
+    Fused epilogue (b200_gemm_bf16_ex): with any of alpha != 1, beta != 0
+    (c: bf16 [M, N], may be `out` itself), bias (bf16 [N]) or
+    out_dtype=torch.float32 the result is
+        out = alpha * (A @ op(B)) + bias + beta * c
+    computed in fp32 from the accumulator, in that order, and written once as
+    out_dtype (bf16 or fp32).
 
     split_k=True lets the tiles of the last, partial wave be split along K
     across CTA pairs (b200_gemm_bf16_ws), which shortens that wave.  It changes
@@ -62,10 +71,30 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.T
         Kb, N = b.shape
     if Kb != K:
         raise ValueError(f"inner dimensions differ: A is {tuple(a.shape)}, B ({b_layout}) is {tuple(b.shape)}")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"out_dtype must be torch.bfloat16 or torch.float32, got {out_dtype}")
+    fused = alpha != 1.0 or beta != 0.0 or bias is not None or out_dtype == torch.float32
+    if fused and split_k:
+        raise ValueError("split_k is not available with a fused epilogue")
+    if beta != 0.0:
+        if c is None:
+            raise ValueError("beta != 0 needs c")
+        _check_operand("c", c)
+        if tuple(c.shape) != (M, N) or c.device != a.device:
+            raise ValueError(f"c must be a [{M}, {N}] tensor on the device of A")
+    if bias is not None:
+        if not isinstance(bias, torch.Tensor) or bias.dtype != torch.bfloat16 or bias.device != a.device \
+                or tuple(bias.shape) != (N,) or (N > 1 and bias.stride(0) != 1):
+            raise ValueError(f"bias must be a contiguous bf16 [{N}] tensor on the device of A")
     if out is None:
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
     else:
-        _check_operand("out", out)
+        if out.dtype != out_dtype:
+            raise TypeError(f"out must be {out_dtype}, got {out.dtype}")
+        if out.dtype == torch.bfloat16:
+            _check_operand("out", out)
+        elif not out.is_cuda or out.dim() != 2 or (out.stride(1) != 1 and out.numel() > 0):
+            raise ValueError("out must be a row-major 2-D CUDA tensor")
         if tuple(out.shape) != (M, N):
             raise ValueError(f"out must have shape {(M, N)}, got {tuple(out.shape)}")
         if out.device != a.device:
@@ -79,6 +108,19 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.T
         torch.cuda.set_device(dev_index)
     try:
         s = stream if stream is not None else torch.cuda.current_stream(a.device)
+        if fused:
+            epi = _lib.Epilogue(alpha=float(alpha), beta=float(beta),
+                                c_in=c.data_ptr() if beta != 0.0 else None,
+                                ldc_in=max(c.stride(0), 1) if beta != 0.0 else 0,
+                                bias=bias.data_ptr() if bias is not None else None,
+                                d_dtype=_lib.B200_DTYPE_F32 if out_dtype == torch.float32 else _lib.B200_DTYPE_BF16)
+            rc = lib.b200_gemm_bf16_ex(
+                ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                M, N, K, max(a.stride(0), 1), max(b.stride(0), 1), max(out.stride(0), 1),
+                layout, ctypes.byref(epi), ctypes.c_void_p(s.cuda_stream))
+            if rc != _lib.B200_OK:
+                raise B200GemmError(rc, f"M={M} N={N} K={K} b_layout={b_layout} (fused epilogue)")
+            return out
         # Split-K workspace for the last wave of tiles (0 bytes when the shape
         # does not need it); torch's caching allocator makes this cheap and
         # stream-safe, so concurrent calls never share a workspace.

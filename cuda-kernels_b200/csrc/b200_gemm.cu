@@ -136,11 +136,13 @@ template <int MPAD>
 int set_skinny_attrs() {
   constexpr int st = SkinnyCfg<MPAD>::kStages;
   constexpr int smem = b200::SkinnySmemPlan<MPAD, st>::kAllocBytes;
-  if (cudaFuncSetAttribute(b200::gemm_bf16_skinny_kernel<MPAD, st, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           smem) != cudaSuccess ||
-      cudaFuncSetAttribute(b200::gemm_bf16_skinny_kernel<MPAD, st, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           smem) != cudaSuccess)
-    return B200_ERR_CUDA;
+  const void* kernels[4] = {(const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, false, false>,
+                            (const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, true, false>,
+                            (const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, false, true>,
+                            (const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, true, true>};
+  for (const void* k : kernels) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return B200_ERR_CUDA;
+  }
   return B200_OK;
 }
 
@@ -155,19 +157,28 @@ int init_device(int dev, DeviceState& st) {
   constexpr int single_smem = b200::SmemPlan<kBN, kStages>::kAllocBytes;
   constexpr int pair_smem = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
   constexpr int wide_smem = b200::PairSmemPlan<kPairWideBN, kPairWideStages>::kAllocBytes;
-  if (cudaFuncSetAttribute(b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, single_smem) != cudaSuccess ||
-      cudaFuncSetAttribute(b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, single_smem) != cudaSuccess ||
-      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess ||
-      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, pair_smem) != cudaSuccess ||
-      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem) != cudaSuccess ||
-      cudaFuncSetAttribute(b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem) != cudaSuccess)
-    return B200_ERR_CUDA;
+  struct KernelSmem {
+    const void* fn;
+    int smem;
+  };
+  const KernelSmem kernels[] = {
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, false>, single_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, false>, single_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, true>, single_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, true>, single_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false, false>, pair_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true, false>, pair_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false, true>, pair_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true, true>, pair_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, false>, wide_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false>, wide_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, true>, wide_smem},
+      {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, true>, wide_smem},
+  };
+  for (const KernelSmem& k : kernels) {
+    if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
+      return B200_ERR_CUDA;
+  }
   if (set_skinny_attrs<16>() != B200_OK || set_skinny_attrs<32>() != B200_OK || set_skinny_attrs<64>() != B200_OK ||
       set_skinny_attrs<128>() != B200_OK)
     return B200_ERR_CUDA;
@@ -227,12 +238,13 @@ struct TmapCache {
 thread_local TmapCache t_tmap_cache;
 
 int encode_2d_uncached(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
-                       uint32_t box_inner, uint32_t box_outer, bool is_load, bool swizzle) {
+                       uint32_t box_inner, uint32_t box_outer, bool is_load, bool swizzle, bool f32) {
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint64_t strides[1] = {pitch_elems * (f32 ? 4 : 2)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         is_load ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -240,20 +252,22 @@ int encode_2d_uncached(CUtensorMap* map, const void* ptr, uint64_t inner, uint64
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
-// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
-// `pitch_elems` elements between rows, box {box_inner, box_outer}, 128B
-// swizzle unless `swizzle` is false.
+// 2-D tensor map (bf16, or fp32 with f32 = true): `inner` contiguous
+// elements per row, `outer` rows, `pitch_elems` elements between rows, box
+// {box_inner, box_outer}, 128B swizzle unless `swizzle` is false.
 int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
-              uint32_t box_inner, uint32_t box_outer, bool is_load, bool swizzle = true) {
+              uint32_t box_inner, uint32_t box_outer, bool is_load, bool swizzle = true, bool f32 = false) {
   TmapCache& c = t_tmap_cache;
-  const TmapKey k{ptr, inner, outer, pitch_elems, box_inner, box_outer, (is_load ? 1u : 0u) | (swizzle ? 2u : 0u)};
+  const TmapKey k{ptr,       inner,     outer,
+                  pitch_elems, box_inner, box_outer,
+                  (is_load ? 1u : 0u) | (swizzle ? 2u : 0u) | (f32 ? 4u : 0u)};
   for (int i = 0; i < kTmapCacheSize; ++i) {
     if (c.used[i] && c.key[i] == k) {
       *map = c.map[i];
       return B200_OK;
     }
   }
-  const int rc = encode_2d_uncached(map, ptr, inner, outer, pitch_elems, box_inner, box_outer, is_load, swizzle);
+  const int rc = encode_2d_uncached(map, ptr, inner, outer, pitch_elems, box_inner, box_outer, is_load, swizzle, f32);
   if (rc == B200_OK) {
     const int i = c.next;
     c.next = (c.next + 1) % kTmapCacheSize;
@@ -269,7 +283,8 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Swap-AB split-K launch for M <= 128 (see gemm_sm100_skinny.cuh).
 template <int MPAD>
 int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
-                  int64_t lda, int64_t ldb, int64_t ldc, int b_layout, cudaStream_t stream) {
+                  int64_t lda, int64_t ldb, int64_t ldc, int b_layout, const b200::EpilogueParams& epi,
+                  cudaStream_t stream) {
   constexpr int stages = SkinnyCfg<MPAD>::kStages;
   using Plan = b200::SkinnySmemPlan<MPAD, stages>;
   CUtensorMap tmB, tmA, tmC;
@@ -305,10 +320,12 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   // C store box: each warp stores [MPAD x 32] without a split; with S splits
   // each CTA stores its owned rows as one [MPAD x 128/S] block.
   const uint32_t box_n = (uint32_t)(splits == 1 ? 32 : b200::kSkinnyBN / splits);
-  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, box_n, MPAD, false, false)) != B200_OK)
+  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, box_n, MPAD, false, false,
+                      epi.out_f32 != 0)) != B200_OK)
     return rc;
   p.timeout_ns = st.timeout_ns;
   p.status = st.status_ptr;
+  p.epi = epi;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -324,10 +341,17 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e =
-      b_layout == B200_B_KN
-          ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, true>, tmB, tmA, tmC, p)
-          : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, false>, tmB, tmA, tmC, p);
+  // The fused-epilogue variants only when needed: the plain ones carry no
+  // epilogue code at all.
+  const bool fused = epi.active || epi.out_f32;
+  cudaError_t e;
+  if (b_layout == B200_B_KN) {
+    e = fused ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, true, true>, tmB, tmA, tmC, p)
+              : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, true, false>, tmB, tmA, tmC, p);
+  } else {
+    e = fused ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, false, true>, tmB, tmA, tmC, p)
+              : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, false, false>, tmB, tmA, tmC, p);
+  }
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -335,8 +359,11 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
 
 namespace {
 
+// `epi` == nullptr: plain GEMM, C = bf16(A op(B)).  Otherwise a validated
+// fused epilogue (see b200_gemm_bf16_ex); C is then D, of its element type.
 int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-              int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes, void* stream_) {
+              int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes, void* stream_,
+              const b200::EpilogueParams* epi_in = nullptr) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
   if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
   const int64_t kLim = 0x7fffffffLL;
@@ -344,7 +371,11 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   if (M == 0 || N == 0) return B200_OK;
   if (C == nullptr) return B200_ERR_INVALID_ARG;
   if (ldc < N) return B200_ERR_INVALID_ARG;
-  if (!aligned16(C) || (ldc % 8) != 0) return B200_ERR_ALIGNMENT;
+  b200::EpilogueParams epi{};
+  epi.alpha = 1.0f;
+  if (epi_in != nullptr) epi = *epi_in;
+  const bool f32 = epi.out_f32 != 0;
+  if (!aligned16(C) || (ldc % (f32 ? 4 : 8)) != 0) return B200_ERR_ALIGNMENT;
 
   DeviceState* st = nullptr;
   int rc = current_device_state(&st);
@@ -352,6 +383,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
 
   if (K == 0) {  // empty reduction: C = 0
+    if (epi.active) return B200_ERR_INVALID_ARG;  // bias / beta * C_in need K >= 1 (no kernel for K = 0)
     return cudaMemset2DAsync(C, (size_t)ldc * 2, 0, (size_t)N * 2, (size_t)M, stream) == cudaSuccess ? B200_OK
                                                                                                       : B200_ERR_CUDA;
   }
@@ -366,10 +398,10 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   const int force = g_force_kernel.load(std::memory_order_relaxed);
   if (force == kForceSkinny && M > 128) return B200_ERR_INVALID_ARG;
   if (force == kForceSkinny || (force == kForceAuto && M <= 128)) {
-    if (M <= 16) return launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
-    if (M <= 32) return launch_skinny<32>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
-    if (M <= 64) return launch_skinny<64>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
-    return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, stream);
+    if (M <= 16) return launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    if (M <= 32) return launch_skinny<32>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    if (M <= 64) return launch_skinny<64>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
   }
   const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM);
   const int max_pairs = st->max_pairs;
@@ -410,8 +442,10 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     rc = encode_2d(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, b200::kBK, true);
   }
   if (rc != B200_OK) return rc;
-  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, b200::kEpiCols, b200::kEpiRowsPerWarp,
-                      false)) != B200_OK)
+  // D store box: 32 rows of one warp x one 128-byte swizzle row (64 bf16 or
+  // 32 fp32 columns).
+  if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, f32 ? 32u : (uint32_t)b200::kEpiCols,
+                      b200::kEpiRowsPerWarp, false, true, f32)) != B200_OK)
     return rc;
 
   const int64_t bm = use_pair ? b200::kPairBM : b200::kBM;
@@ -429,14 +463,18 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   p.b_mn_major = (b_layout == B200_B_KN) ? 1u : 0u;
   p.timeout_ns = st->timeout_ns;
   p.status = st->status_ptr;
+  p.epi = epi;
 
   if (!use_pair) {
     p.sk_first = p.num_work = p.num_tiles;
     p.sk_parts = 1;
     p.sk_kpp = p.num_k_blk;
     const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
-    auto kern = p.b_mn_major ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true>
-                             : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false>;
+    const bool fused = epi.active || epi.out_f32;
+    auto kern = p.b_mn_major ? (fused ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, true>
+                                      : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, false>)
+                             : (fused ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, true>
+                                      : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, false>);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -487,16 +525,20 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e;
-  if (use_wide) {
-    e = p.b_mn_major
-            ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true>, tmA, tmB, tmC, p)
-            : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false>, tmA, tmB, tmC,
-                                 p);
-  } else {
-    e = p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true>, tmA, tmB, tmC, p)
-                     : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false>, tmA, tmB, tmC, p);
-  }
+  // Pick the instantiation: tile width x B layout x (plain | fused epilogue).
+  using PairKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const b200::GemmParams);
+  static const PairKernel kPair[2][2][2] = {
+      {{b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false, false>,
+        b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false, true>},
+       {b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true, false>,
+        b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true, true>}},
+      {{b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, false>,
+        b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, true>},
+       {b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false>,
+        b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, true>}}};
+  const bool fused = epi.active || epi.out_f32;
+  const PairKernel kern = kPair[use_wide ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -513,6 +555,32 @@ extern "C" B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C,
   if (workspace == nullptr && workspace_bytes != 0) return B200_ERR_INVALID_ARG;
   if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) != 0) return B200_ERR_ALIGNMENT;
   return gemm_impl(A, B, C, M, N, K, lda, ldb, ldc, b_layout, workspace, workspace_bytes, stream);
+}
+
+extern "C" B200_API int b200_gemm_bf16_ex(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
+                                          int64_t lda, int64_t ldb, int64_t ldd, int b_layout, const b200_epilogue* epi,
+                                          void* stream) {
+  if (epi == nullptr) return gemm_impl(A, B, D, M, N, K, lda, ldb, ldd, b_layout, nullptr, 0, stream);
+  if (epi->d_dtype != B200_DTYPE_BF16 && epi->d_dtype != B200_DTYPE_F32) return B200_ERR_INVALID_ARG;
+  b200::EpilogueParams e{};
+  e.alpha = epi->alpha;
+  e.beta = epi->beta;
+  e.out_f32 = epi->d_dtype == B200_DTYPE_F32 ? 1u : 0u;
+  if (epi->bias != nullptr) {
+    if (!aligned16(epi->bias)) return B200_ERR_ALIGNMENT;
+    e.bias = static_cast<const __nv_bfloat16*>(epi->bias);
+  }
+  if (epi->beta != 0.0f) {
+    if (epi->c_in == nullptr || epi->ldc_in < N) return B200_ERR_INVALID_ARG;
+    if (!aligned16(epi->c_in) || (epi->ldc_in % 8) != 0) return B200_ERR_ALIGNMENT;
+    // In place (C_in = D) only when D is bf16 with the same pitch: every
+    // element is read before it is overwritten, by the thread that writes it.
+    if (epi->c_in == D && (e.out_f32 || epi->ldc_in != ldd)) return B200_ERR_INVALID_ARG;
+    e.c_in = static_cast<const __nv_bfloat16*>(epi->c_in);
+    e.ldc_in = epi->ldc_in;
+  }
+  e.active = (e.alpha != 1.0f || e.beta != 0.0f || e.bias != nullptr) ? 1u : 0u;
+  return gemm_impl(A, B, D, M, N, K, lda, ldb, ldd, b_layout, nullptr, 0, stream, &e);
 }
 
 extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {

@@ -43,6 +43,105 @@ constexpr int kEpiCols = 64;             // columns per epilogue chunk (one 128B
 constexpr int kEpiRowsPerWarp = 32;
 constexpr int kEpiBufBytes = kEpiRowsPerWarp * kEpiCols * 2;  // 4 KiB
 
+// Optional fused epilogue (b200_gemm_bf16_ex): D = alpha * acc + bias[n] +
+// beta * C_in[m, n], rounded to bf16 or kept in fp32.  The operations are
+// done one at a time in fp32, in that order, without contraction into FMAs,
+// so a CPU restatement reproduces them exactly from the same fp32 acc.
+// `active` == 0 is the plain GEMM (D = bf16(acc)) with no extra work.
+struct EpilogueParams {
+  const __nv_bfloat16* c_in;  // [M, N] row-major, leading dimension ldc_in; read only when beta != 0
+  const __nv_bfloat16* bias;  // [N] or nullptr
+  int64_t ldc_in;
+  float alpha, beta;
+  uint32_t out_f32;  // element type of D: 0 bf16, 1 fp32
+  uint32_t active;
+};
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+// 32 consecutive columns n0 .. n0+31 of row m, held by one thread as fp32
+// bit patterns: apply the epilogue in place, 8 columns (one 16-byte load of
+// bias and of C_in) at a time.  Columns >= N and rows >= M read nothing
+// (their results are never stored).  C_in is read with plain loads: it may be
+// D itself, whose other elements TMA stores are writing meanwhile.
+__device__ __forceinline__ void epilogue_row32(uint32_t (&v)[32], const EpilogueParams& e, int m, int n0, int M,
+                                               int N) {
+  const bool use_c = e.beta != 0.0f && m < M;
+  const unsigned short* bias = reinterpret_cast<const unsigned short*>(e.bias);
+  const unsigned short* crow =
+      use_c ? reinterpret_cast<const unsigned short*>(e.c_in) + (size_t)m * (size_t)e.ldc_in : nullptr;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int n = n0 + 8 * g;
+    uint32_t bw[4] = {0u, 0u, 0u, 0u}, cw[4] = {0u, 0u, 0u, 0u};
+    if (n + 8 <= N) {
+      if (bias != nullptr) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(bias + n));
+        bw[0] = w.x; bw[1] = w.y; bw[2] = w.z; bw[3] = w.w;
+      }
+      if (use_c) {
+        const uint4 w = ld_global_v4_u32(crow + n);
+        cw[0] = w.x; cw[1] = w.y; cw[2] = w.z; cw[3] = w.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (n + i < N) {
+          const uint32_t sh = (i & 1) * 16u;
+          if (bias != nullptr) bw[i >> 1] |= (uint32_t)__ldg(bias + n + i) << sh;
+          if (use_c) cw[i >> 1] |= ld_global_u16(crow + n + i) << sh;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b16 = (bw[i >> 1] >> ((i & 1) * 16u)) & 0xffffu;
+      const uint32_t c16 = (cw[i >> 1] >> ((i & 1) * 16u)) & 0xffffu;
+      float x = __fmul_rn(e.alpha, __uint_as_float(v[8 * g + i]));
+      x = __fadd_rn(x, bf16_bits_to_f32(b16));
+      x = __fadd_rn(x, __fmul_rn(e.beta, bf16_bits_to_f32(c16)));
+      v[8 * g + i] = __float_as_uint(x);
+    }
+  }
+}
+
+// Stage one thread's 64 columns (lo = columns 0..31, hi = 32..63) of a warp's
+// 32-row block into 128B-swizzled shared memory for the TMA store of D.
+// bf16 D: one 4 KiB buffer [32 rows][64 cols].  fp32 D: two 4 KiB buffers
+// [32 rows][32 cols] (lo into buf0, hi into buf1).
+__device__ __forceinline__ void stage_row64(const uint32_t (&lo)[32], const uint32_t (&hi)[32], bool f32,
+                                            uint32_t buf0, uint32_t buf1, uint32_t lane) {
+  if (!f32) {
+    const uint32_t row_addr = buf0 + lane * 128u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* src = (j < 4) ? &lo[j * 8] : &hi[(j - 4) * 8];
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(src[2 * e]), __uint_as_float(src[2 * e + 1]));
+        w[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                   : "memory");
+    }
+  } else {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t* src = half == 0 ? lo : hi;
+      const uint32_t row_addr = (half == 0 ? buf0 : buf1) + lane * 128u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(src[4 * j]), "r"(src[4 * j + 1]),
+                     "r"(src[4 * j + 2]), "r"(src[4 * j + 3])
+                     : "memory");
+      }
+    }
+  }
+}
+
 struct GemmParams {
   int32_t M, N, K;
   int32_t num_m_blk, num_n_blk, num_k_blk;
@@ -61,6 +160,7 @@ struct GemmParams {
   uint32_t* status;      // device status word (DeviceStatus bits), OR-ed on failure
   float* workspace;      // [split tiles][sk_parts-1][2 CTAs][BN/4][128][4] fp32
   uint64_t* flags;       // [split tiles][sk_parts-1][2 CTAs]
+  EpilogueParams epi;
 };
 
 template <int BN, int STAGES>
@@ -122,7 +222,7 @@ __device__ __forceinline__ void raise_status(const GemmParams& p, volatile uint3
   if (p.status != nullptr) atomicOr(p.status, code);
 }
 
-template <int BN, int STAGES, bool B_MN>
+template <int BN, int STAGES, bool B_MN, bool EPI = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -321,28 +421,32 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(acce_bar(acc));
         }
-        const uint32_t buf = sC + (uint32_t)((slot * 2 + sbuf) * kEpiBufBytes);
-        if (lane == 0) bulk_wait_group_read<1>();  // the store that used `buf` has read it
-        __syncwarp();
-        const uint32_t row_addr = buf + lane * 128u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* src = (j < 4) ? &r0[j * 8] : &r1[(j - 4) * 8];
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(src[2 * e]), __uint_as_float(src[2 * e + 1]));
-            w[e] = *reinterpret_cast<uint32_t*>(&h);
+        const int n0 = nb * BN + c * kEpiCols;
+        const int m0 = mb * kBM + q * kEpiRowsPerWarp;
+        if constexpr (EPI) {
+          if (p.epi.active) {
+            epilogue_row32(r0, p.epi, m0 + (int)lane, n0, p.M, p.N);
+            epilogue_row32(r1, p.epi, m0 + (int)lane, n0 + 32, p.M, p.N);
           }
-          const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                       "r"(w[3])
-                       : "memory");
         }
+        const bool f32 = EPI && p.epi.out_f32 != 0;
+        // bf16 D alternates the warp's two buffers; fp32 D uses both per chunk.
+        const uint32_t buf0 = sC + (uint32_t)((slot * 2 + (f32 ? 0 : sbuf)) * kEpiBufBytes);
+        const uint32_t buf1 = sC + (uint32_t)((slot * 2 + 1) * kEpiBufBytes);
+        if (lane == 0) {
+          if (f32) {
+            bulk_wait_group_read<0>();
+          } else {
+            bulk_wait_group_read<1>();  // the store that used `buf0` has read it
+          }
+        }
+        __syncwarp();
+        stage_row64(r0, r1, f32, buf0, buf1, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf, nb * BN + c * kEpiCols, mb * kBM + q * kEpiRowsPerWarp);
+          tma_store_2d(&tmC, buf0, n0, m0);
+          if (f32) tma_store_2d(&tmC, buf1, n0 + 32, m0);
           bulk_commit_group();
         }
         sbuf ^= 1;

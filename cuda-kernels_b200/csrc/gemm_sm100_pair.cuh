@@ -68,7 +68,7 @@ struct PairSmemPlan {
   static_assert(kAccN * BN <= kTmemCols, "accumulators must fit in TMEM");
 };
 
-template <int BN, int STAGES, bool B_MN>
+template <int BN, int STAGES, bool B_MN, bool EPI = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -344,28 +344,31 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
           }
         }
-        const uint32_t buf = sC + (uint32_t)((slot * 2 + sbuf) * kEpiBufBytes);
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t row_addr = buf + lane * 128u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* src = (j < 4) ? &r0[j * 8] : &r1[(j - 4) * 8];
-          uint32_t wv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(src[2 * e]), __uint_as_float(src[2 * e + 1]));
-            wv[e] = *reinterpret_cast<uint32_t*>(&h);
+        const int n0 = wk.nb * BN + c * kEpiCols;
+        if constexpr (EPI) {
+          if (p.epi.active) {
+            epilogue_row32(r0, p.epi, row + (int)lane, n0, p.M, p.N);
+            epilogue_row32(r1, p.epi, row + (int)lane, n0 + 32, p.M, p.N);
           }
-          const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(wv[0]), "r"(wv[1]), "r"(wv[2]),
-                       "r"(wv[3])
-                       : "memory");
         }
+        const bool f32 = EPI && p.epi.out_f32 != 0;
+        // bf16 D alternates the warp's two buffers; fp32 D uses both per chunk.
+        const uint32_t buf0 = sC + (uint32_t)((slot * 2 + (f32 ? 0 : sbuf)) * kEpiBufBytes);
+        const uint32_t buf1 = sC + (uint32_t)((slot * 2 + 1) * kEpiBufBytes);
+        if (lane == 0) {
+          if (f32) {
+            bulk_wait_group_read<0>();
+          } else {
+            bulk_wait_group_read<1>();  // the store that used `buf0` has read it
+          }
+        }
+        __syncwarp();
+        stage_row64(r0, r1, f32, buf0, buf1, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf, wk.nb * BN + c * kEpiCols, row);
+          tma_store_2d(&tmC, buf0, n0, row);
+          if (f32) tma_store_2d(&tmC, buf1, n0 + 32, row);
           bulk_commit_group();
         }
         sbuf ^= 1;

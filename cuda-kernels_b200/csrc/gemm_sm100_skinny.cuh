@@ -38,6 +38,7 @@ struct SkinnyParams {
   int32_t splits;        // S = cluster size along x: 1, 2, 4 or 8
   uint64_t timeout_ns;
   uint32_t* status;
+  EpilogueParams epi;  // fused epilogue (element [m, n] of D; see gemm_sm100.cuh)
 };
 
 template <int MPAD, int STAGES>
@@ -64,8 +65,9 @@ struct SkinnySmemPlan {
   //                      staged locally, the others arrive by bulk copy);
   //   [recv, cstage)     this CTA's partials of the rows the others own
   //                      ([S-1][R][kPitch] fp32), one bulk copy per owner;
-  //   [cstage, ...)      the bf16 C block of the owned rows, [MPAD][R].
-  // S == 1: four per-warp bf16 C tiles [MPAD][32] at the start of the ring.
+  //   [cstage, ...)      the D block of the owned rows, [MPAD][R] (bf16
+  //                      or fp32).
+  // S == 1: four per-warp D tiles [MPAD][32] at the start of the ring.
   static constexpr int kPitch = MPAD + 4;
   __host__ __device__ static constexpr int block_bytes(int S) { return (kSkinnyBN / S) * kPitch * 4; }
   __host__ __device__ static constexpr int recv_bytes(int S) { return S * block_bytes(S); }
@@ -73,7 +75,7 @@ struct SkinnySmemPlan {
     return S > 1 ? (recv_bytes(S) + (S - 1) * block_bytes(S) + 1023) & ~1023 : 0;
   }
   __host__ __device__ static constexpr int cstage_bytes(int S) {
-    return S > 1 ? MPAD * (kSkinnyBN / S) * 2 : 4 * MPAD * 32 * 2;
+    return S > 1 ? MPAD * (kSkinnyBN / S) * 4 : 4 * MPAD * 32 * 4;  // room for fp32 D
   }
   __host__ __device__ static constexpr bool fits(int S) { return cstage_off(S) + cstage_bytes(S) <= kRingBytes; }
   // Largest power-of-two split count (<= 8) whose reduction scratch fits.
@@ -82,6 +84,30 @@ struct SkinnySmemPlan {
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 256, "UMMA N must be 16..256 in steps of 16");
 };
 
+// Fused epilogue for element [m, n] of D (one fp32 accumulator value x):
+// same operations and order as epilogue_row32.
+__device__ __forceinline__ float skinny_epi(float x, const EpilogueParams& e, int m, int n, int M, int N,
+                                            float bias_n) {
+  x = __fmul_rn(e.alpha, x);
+  x = __fadd_rn(x, bias_n);
+  float c = 0.0f;
+  if (e.beta != 0.0f && m < M && n < N) {
+    c = bf16_bits_to_f32(ld_global_u16(e.c_in + (size_t)m * (size_t)e.ldc_in + n));
+  }
+  return __fadd_rn(x, __fmul_rn(e.beta, c));
+}
+
+// Writes D element (one fp32 value) into a staging tile as bf16 or fp32.
+__device__ __forceinline__ void skinny_stage(uint32_t addr_elem0, int idx, float x, bool f32) {
+  if (f32) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr_elem0 + (uint32_t)(idx * 4)), "f"(x) : "memory");
+  } else {
+    const __nv_bfloat16 hv = __float2bfloat16_rn(x);
+    const uint16_t hb = *reinterpret_cast<const uint16_t*>(&hv);
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr_elem0 + (uint32_t)(idx * 2)), "h"(hb) : "memory");
+  }
+}
+
 __device__ __forceinline__ void skinny_raise(const SkinnyParams& p, volatile uint32_t* abort_flag, uint32_t code) {
   *abort_flag = 1u;
   if (p.status != nullptr) atomicOr(p.status, code);
@@ -89,7 +115,7 @@ __device__ __forceinline__ void skinny_raise(const SkinnyParams& p, volatile uin
 
 // Grid: (S, ceil(N/128)); cluster (S, 1, 1).  CTA rank r of cluster y handles
 // N rows [128y, 128y+128) and K-blocks [r*kb_per_split, (r+1)*kb_per_split).
-template <int MPAD, int STAGES, bool B_MN>
+template <int MPAD, int STAGES, bool B_MN, bool EPI = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_skinny_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmC, const SkinnyParams p) {
@@ -288,15 +314,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // Whole tile here: each warp rounds its 32 rows and stores them as one
     // [MPAD x 32] block of C.
     if (epi && have_acc) {
-      const uint32_t stage_buf = base + (uint32_t)(slot * MPAD * 32 * 2);
+      const bool f32 = EPI && p.epi.out_f32 != 0;
+      const uint32_t stage_buf = base + (uint32_t)(slot * MPAD * 32 * (f32 ? 4 : 2));
+      const int n = n0 + row;  // weight row = column n of D
+      float bias_n = 0.0f;
+      if (EPI && p.epi.active && p.epi.bias != nullptr && n < p.N) {
+        bias_n = bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p.epi.bias) + n));
+      }
       for_each_chunk([&](int c, const uint32_t (&v)[kChunk]) {
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
-          const __nv_bfloat16 hv = __float2bfloat16_rn(__uint_as_float(v[j]));
-          const uint16_t hb = *reinterpret_cast<const uint16_t*>(&hv);
-          asm volatile("st.shared.b16 [%0], %1;" ::"r"(stage_buf + (uint32_t)(((c + j) * 32 + (int)lane) * 2)),
-                       "h"(hb)
-                       : "memory");
+          float x = __uint_as_float(v[j]);
+          if constexpr (EPI) {
+            if (p.epi.active) x = skinny_epi(x, p.epi, c + j, n, p.M, p.N, bias_n);
+          }
+          skinny_stage(stage_buf, (c + j) * 32 + (int)lane, x, f32);
         }
       });
       fence_proxy_async_smem();
@@ -374,16 +406,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   cluster_arrive();  // #2
   if (epi && go) {
     // Sum the S partials of the owned rows in split order (deterministic),
-    // round to bf16 and stage C[m, n0 + rank*R + r] as [MPAD][R].  The 128
+    // apply the epilogue, stage D[m, n0 + rank*R + r] as [MPAD][R].  The 128
     // epilogue threads split the block: thread t takes row t % R and CPT
     // consecutive columns.
     constexpr int kMinCpt = 4;
     const int cpt = max(kMinCpt, MPAD * R / (kEpiWarps * 32));
     const int groups = MPAD / cpt;
     const int t = (int)threadIdx.x - 64;
+    const bool f32 = EPI && p.epi.out_f32 != 0;
     if (t < R * groups) {
       const int r = t % R;
       const int c0 = (t / R) * cpt;
+      const int n = n0 + (int)rank * R + r;  // column n of D
+      float bias_n = 0.0f;
+      if (EPI && p.epi.active && p.epi.bias != nullptr && n < p.N) {
+        bias_n = bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p.epi.bias) + n));
+      }
 #pragma unroll 2
       for (int c = c0; c < c0 + cpt; c += 4) {
         // All S loads first (independent), then the sum in split order.
@@ -408,10 +446,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const __nv_bfloat16 hv = __float2bfloat16_rn(a[j]);
-          const uint16_t hb = *reinterpret_cast<const uint16_t*>(&hv);
-          asm volatile("st.shared.b16 [%0], %1;" ::"r"(cstage + (uint32_t)(((c + j) * R + r) * 2)), "h"(hb)
-                       : "memory");
+          float x = a[j];
+          if constexpr (EPI) {
+            if (p.epi.active) x = skinny_epi(x, p.epi, c + j, n, p.M, p.N, bias_n);
+          }
+          skinny_stage(cstage, (c + j) * R + r, x, f32);
         }
       }
     }

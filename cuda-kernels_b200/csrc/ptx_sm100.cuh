@@ -169,6 +169,18 @@ __device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t threads, boo
       : "memory");
   return r != 0;
 }
+// Plain (coherent) global loads, for data this kernel may also write through
+// another path (C_in aliasing D); never the read-only cache.
+__device__ __forceinline__ uint4 ld_global_v4_u32(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_global_u16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c, float d) {
   asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }

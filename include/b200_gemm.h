@@ -96,6 +96,39 @@ B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M,
                                int64_t ldb, int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/* Element type of D for b200_gemm_bf16_ex. */
+#define B200_DTYPE_BF16 0
+#define B200_DTYPE_F32 1
+
+/*
+ * Fused epilogue: D[m, n] = alpha * (A op(B))[m, n] + bias[n] + beta * c_in[m, n],
+ * computed in fp32 from the fp32 accumulator, one operation at a time in that
+ * order (no fused multiply-add), then stored as d_dtype.
+ */
+typedef struct b200_epilogue {
+  float alpha;       /* scale of the product (1 for none) */
+  float beta;        /* scale of c_in; 0 = c_in is not read */
+  const void* c_in;  /* bf16 [M, N] row-major, leading dimension ldc_in (>= N, multiple of 8), 16-byte aligned;
+                        may be D itself (in-place accumulate) when D is bf16 with ldd == ldc_in */
+  int64_t ldc_in;
+  const void* bias;  /* bf16 [N], 16-byte aligned, added to every row; NULL for none */
+  int d_dtype;       /* B200_DTYPE_BF16 or B200_DTYPE_F32 */
+} b200_epilogue;
+
+/*
+ * b200_gemm_bf16 with a fused epilogue (bias, residual / beta * C, alpha,
+ * fp32 output) applied to the fp32 accumulator before D is written once.
+ * D is [M, N] of d_dtype with leading dimension ldd elements (bf16: multiple
+ * of 8; fp32: multiple of 4), 16-byte aligned.  epi == NULL is exactly
+ * b200_gemm_bf16.  K must be >= 1 when an epilogue is given
+ * (B200_ERR_INVALID_ARG otherwise).  Always sequential K order (no split-K).
+ * No reference counterpart: the reference's kernels write only
+ * C = bf16(A * B^T) (bf16_matmul/matmul_v8_tuned.cu:152-178); this is the
+ * epilogue fusion its callers would otherwise do with extra passes over C.
+ */
+B200_API int b200_gemm_bf16_ex(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, int64_t ldd, int b_layout, const b200_epilogue* epi, void* stream);
+
 /*
  * Workspace b200_gemm_bf16_ws wants for this shape on the current device
  * (0 when it would not split; at most ~19 MB on a B200).  Depends on the

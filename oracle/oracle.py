@@ -123,6 +123,27 @@ def bf16_to_f32(x: np.ndarray) -> np.ndarray:
     return y
 
 
+def epilogue(acc: np.ndarray, alpha: float = 1.0, beta: float = 0.0, c_in: np.ndarray | None = None,
+             bias: np.ndarray | None = None, out: str = "bf16") -> np.ndarray:
+    """Fused epilogue of b200_gemm_bf16_ex on an fp32 accumulator `acc` [M, N]:
+    D = alpha * acc + bias[n] + beta * c_in[m, n], one fp32 operation at a
+    time in that order (no fused multiply-add), then RN-even bf16 (uint16
+    bits) or fp32.  bias / c_in are bf16 bit patterns.  The reference has no
+    epilogue (its kernels store bf16(acc) only, bf16_matmul/matmul_v8_tuned.cu:
+    152-178); this restates the documented semantics of the new entry point.
+    Also used on the fp64 product (acc float64) for a near-exact reference."""
+    ft = np.float64 if acc.dtype == np.float64 else np.float32
+    acc = np.asarray(acc, dtype=ft)
+    x = (ft(alpha) * acc).astype(ft)
+    bvec = bf16_to_f32(bias).astype(ft) if bias is not None else np.zeros(acc.shape[1], dtype=ft)
+    x = (x + bvec[None, :]).astype(ft)
+    cmat = bf16_to_f32(c_in).astype(ft) if (c_in is not None and beta != 0.0) else np.zeros_like(x)
+    x = (x + (ft(beta) * cmat).astype(ft)).astype(ft)
+    if out == "f32" or ft == np.float64:
+        return x
+    return f32_to_bf16(x)
+
+
 # --- the reference's own kernel (oracle/_ref), GPU only ---------------------
 
 def ref_available() -> bool:

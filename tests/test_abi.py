@@ -85,3 +85,25 @@ def test_torch_binding_rejects_bad_arguments_on_cpu():
         ext.matmul_b200(a.float(), a)
     with pytest.raises(ValueError, match="bfloat16"):
         ext.matmul_b200_kn(a.half(), a)
+
+
+def test_epilogue_argument_errors_without_gpu():
+    from b200_gemm import _lib
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    fake = P(0x10000)
+    bad_dtype = _lib.Epilogue(alpha=1.0, beta=0.0, c_in=None, ldc_in=0, bias=None, d_dtype=7)
+    assert lib.b200_gemm_bf16_ex(fake, fake, fake, 8, 8, 8, 8, 8, 8, 0, ctypes.byref(bad_dtype),
+                                 None) == _lib.B200_ERR_INVALID_ARG
+    odd_bias = _lib.Epilogue(alpha=1.0, beta=0.0, c_in=None, ldc_in=0, bias=0x10002, d_dtype=0)
+    assert lib.b200_gemm_bf16_ex(fake, fake, fake, 8, 8, 8, 8, 8, 8, 0, ctypes.byref(odd_bias),
+                                 None) == _lib.B200_ERR_ALIGNMENT
+    no_c = _lib.Epilogue(alpha=1.0, beta=1.0, c_in=None, ldc_in=8, bias=None, d_dtype=0)
+    assert lib.b200_gemm_bf16_ex(fake, fake, fake, 8, 8, 8, 8, 8, 8, 0, ctypes.byref(no_c),
+                                 None) == _lib.B200_ERR_INVALID_ARG
+    short_ld = _lib.Epilogue(alpha=1.0, beta=1.0, c_in=0x20000, ldc_in=4, bias=None, d_dtype=0)
+    assert lib.b200_gemm_bf16_ex(fake, fake, fake, 8, 8, 8, 8, 8, 8, 0, ctypes.byref(short_ld),
+                                 None) == _lib.B200_ERR_INVALID_ARG
+    f32_alias = _lib.Epilogue(alpha=1.0, beta=1.0, c_in=0x10000, ldc_in=8, bias=None, d_dtype=1)
+    assert lib.b200_gemm_bf16_ex(fake, fake, fake, 8, 8, 8, 8, 8, 8, 0, ctypes.byref(f32_alias),
+                                 None) == _lib.B200_ERR_INVALID_ARG

@@ -26,6 +26,20 @@ def test_bf16_rounding_known_answers():
     assert back.tolist() == [1.0, 1.0, 1.0 + 2 ** -6, 1.0 + 2 ** -7, -1.0]
 
 
+def test_epilogue_known_answers():
+    # D = alpha * acc + bias + beta * c_in, one fp32 operation at a time.
+    acc = np.array([[1.5, -0.0, 3.0, 1.0]], dtype=np.float32)
+    bias = o.f32_to_bf16(np.array([0.25, 0.0, -1.0, 2 ** -8], dtype=np.float32))
+    c_in = o.f32_to_bf16(np.array([[1.0, 2.0, 0.5, 0.0]], dtype=np.float32))
+    got = o.epilogue(acc, 2.0, 0.5, c_in, bias)
+    # 2*1.5+0.25+0.5 = 3.75; -0+0+1 = 1; 6-1+0.25 = 5.25; 2+2^-8 -> RN-even tie down to 2.0
+    assert [hex(v) for v in got.ravel()] == ["0x4070", "0x3f80", "0x40a8", "0x4000"]
+    f = o.epilogue(acc, 2.0, 0.5, c_in, bias, out="f32")
+    assert f.dtype == np.float32 and f.ravel().tolist() == [3.75, 1.0, 5.25, 2.0 + 2 ** -8]
+    # no bias, beta = 0: only the scale; c_in is not read
+    assert o.epilogue(acc, 0.5, 0.0, None, None, out="f32").ravel().tolist() == [0.75, 0.0, 1.5, 0.5]
+
+
 def test_tiny_known_product():
     # 2x3 @ (2x3)^T with exactly representable values.
     a = o.f32_to_bf16(np.array([[1, 2, 3], [-1, 0.5, 4]], dtype=np.float32))
