@@ -308,6 +308,101 @@ def time_config(M, N, K, layout, dist_kind, b200_gemm, target_ms=250.0, warmup=1
     return res
 
 
+def _time_variants(fns, target_ms=250.0, warmup=10, use_graph=True):
+    """Device time per call of each fn(i) (i picks the rotating buffer set), back to back;
+    graph replay for calls under 1 ms so host launch cost is not timed."""
+    import torch
+    res = {}
+    for name, fn in fns.items():
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(3):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        est = max(e0.elapsed_time(e1) / 3, 1e-3)
+        if use_graph and est < 1.0:
+            per = max(8, int(2.0 / est))
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                fn(0)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(graph, stream=s):
+                    for i in range(per):
+                        fn(i)
+            torch.cuda.synchronize()
+            graph.replay()
+            torch.cuda.synchronize()
+            reps = max(3, int(target_ms / (est * per)))
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = e0.elapsed_time(e1) / (reps * per)
+            del graph
+            continue
+        steps = max(5, int(target_ms / est))
+        e0.record()
+        for i in range(steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / steps
+    return res
+
+
+def run_epilogue(args) -> int:
+    """--epilogue: the fused epilogue (b200_gemm_bf16_ex) against the same result
+    computed unfused (plain GEMM, then bias and residual adds as separate
+    passes over C), and cuBLAS's own fused bias (torch.addmm) + residual add.
+    One JSON line per shape; device time per call, rotating inputs > L2."""
+    import math
+    import torch
+    torch.cuda.set_device(0)
+    import b200_gemm
+    dev = torch.device("cuda", 0)
+    shapes = [(4096, 4096, 4096), (8192, 4096, 4096), (128, 14336, 4096), (16, 4096, 4096)]
+    for (M, N, K) in shapes:
+        set_bytes = 2 * (M * K + K * N + 2 * M * N)
+        R = max(2, math.ceil(400e6 / set_bytes))
+        g = torch.Generator(device=dev).manual_seed(M + N + K)
+        A = [torch.randn((M, K), generator=g, device=dev).bfloat16() for _ in range(R)]
+        B = [(torch.randn((K, N), generator=g, device=dev) * K ** -0.5).bfloat16() for _ in range(R)]
+        Res = [torch.randn((M, N), generator=g, device=dev).bfloat16() for _ in range(R)]
+        C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(R)]
+        C32 = torch.empty((M, N), dtype=torch.float32, device=dev)
+        bias = torch.randn((N,), generator=g, device=dev).bfloat16()
+        fns = {
+            "plain": lambda i: b200_gemm.gemm(A[i % R], B[i % R], b_layout="kn", out=C[i % R]),
+            "fused_bias_residual": lambda i: b200_gemm.gemm(A[i % R], B[i % R], b_layout="kn", out=C[i % R],
+                                                            beta=1.0, c=Res[i % R], bias=bias),
+            "unfused_bias_residual": lambda i: (b200_gemm.gemm(A[i % R], B[i % R], b_layout="kn", out=C[i % R]),
+                                                C[i % R].add_(bias), C[i % R].add_(Res[i % R])),
+            "fused_f32_out": lambda i: b200_gemm.gemm(A[i % R], B[i % R], b_layout="kn", out=C32,
+                                                      out_dtype=torch.float32),
+            "cublas_addmm_bias_plus_residual": lambda i: (torch.addmm(bias, A[i % R], B[i % R], out=C[i % R]),
+                                                          C[i % R].add_(Res[i % R])),
+        }
+        t = _time_variants(fns, target_ms=args.target_ms)
+        b200_gemm.check_status()
+        flops = 2.0 * M * N * K
+        line = {"what": "fused_epilogue", "config": {"M": M, "N": N, "K": K, "b_layout": "kn", "data": "normal"},
+                "us": {k: round(v * 1e3, 2) for k, v in t.items()},
+                "tflops": {k: round(flops / (v / 1e3) / 1e12, 1) for k, v in t.items()},
+                "fused_vs_unfused": round(t["unfused_bias_residual"] / t["fused_bias_residual"], 3),
+                "fused_vs_cublas_addmm": round(t["cublas_addmm_bias_plus_residual"] / t["fused_bias_residual"], 3)}
+        print(json.dumps(line), flush=True)
+        del A, B, Res, C, C32
+        torch.cuda.empty_cache()
+    return 0
+
+
 def run_sweep(args) -> int:
     """--sweep: one JSON line per single-GPU BASELINE config (b200 and cuBLAS, same loop)."""
     import torch
@@ -460,6 +555,7 @@ def main(argv=None) -> int:
     ap.add_argument("--dist", default="normal", choices=["normal", "uniform"])
     ap.add_argument("--target-ms", type=float, default=250.0)
     ap.add_argument("--rowshard", action="store_true", help="BASELINE config 5: row-sharded 131072x8192x8192")
+    ap.add_argument("--epilogue", action="store_true", help="fused epilogue vs unfused and vs cuBLAS addmm")
     ap.add_argument("--rowshard-m", type=int, default=131072)
     ap.add_argument("--chunks", type=int, default=1, help="--rowshard: column chunks of B broadcast one by one")
     args = ap.parse_args(argv)
@@ -467,6 +563,8 @@ def main(argv=None) -> int:
         return run_rowshard(args)
     if args.shape:
         return run_shape(args)
+    if args.epilogue:
+        return run_epilogue(args)
     if args.sweep:
         return run_sweep(args)
     if args.warmup < 3:

@@ -136,12 +136,15 @@ template <int MPAD>
 int set_skinny_attrs() {
   constexpr int st = SkinnyCfg<MPAD>::kStages;
   constexpr int smem = b200::SkinnySmemPlan<MPAD, st>::kAllocBytes;
+  constexpr int smem_epi = b200::SkinnySmemPlan<MPAD, st>::kAllocBytesEpi;
   const void* kernels[4] = {(const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, false, false>,
                             (const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, true, false>,
                             (const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, false, true>,
                             (const void*)b200::gemm_bf16_skinny_kernel<MPAD, st, true, true>};
-  for (const void* k : kernels) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return B200_ERR_CUDA;
+  for (int i = 0; i < 4; ++i) {
+    if (cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, i < 2 ? smem : smem_epi) !=
+        cudaSuccess)
+      return B200_ERR_CUDA;
   }
   return B200_OK;
 }
@@ -337,13 +340,13 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3((unsigned)splits, (unsigned)n_tiles, 1);
   cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
-  cfg.dynamicSmemBytes = Plan::kAllocBytes;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
   // The fused-epilogue variants only when needed: the plain ones carry no
   // epilogue code at all.
   const bool fused = epi.active || epi.out_f32;
+  cfg.dynamicSmemBytes = fused ? Plan::kAllocBytesEpi : Plan::kAllocBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   cudaError_t e;
   if (b_layout == B200_B_KN) {
     e = fused ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_skinny_kernel<MPAD, stages, true, true>, tmB, tmA, tmC, p)
@@ -426,7 +429,11 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     const int64_t rounds = (t + max_pairs - 1) / max_pairs;
     return ((double)t / (double)(rounds * max_pairs)) * ((double)N / (double)(n_blk * bn_));
   };
-  const bool use_wide = use_pair && !use_split &&
+  // A fused epilogue does more work per tile (C_in loads, fp32 stores); the
+  // wide tile's single TMEM accumulator would expose it, the 256-column
+  // tiles' double-buffered accumulators hide it behind the next tile.
+  const bool fused_epi = epi.active || epi.out_f32;
+  const bool use_wide = use_pair && !use_split && !fused_epi &&
                         m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= max_pairs &&
                         wave_eff(kPairWideBN) >= 0.97 * wave_eff(kPairBN);
   const uint32_t bn = !use_pair ? (uint32_t)kBN : use_wide ? (uint32_t)kPairWideBN : (uint32_t)kPairBN;

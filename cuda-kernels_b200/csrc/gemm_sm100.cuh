@@ -142,6 +142,17 @@ __device__ __forceinline__ void stage_row64(const uint32_t (&lo)[32], const uint
   }
 }
 
+// Epilogue helper: while the tile's MMAs still run, pull this thread's row
+// segment of C_in, columns [n0, n0 + cols), into L2 (clipped to N; the size
+// is rounded up to 8 elements, which stays inside the row since ldc_in is a
+// multiple of 8 and >= N).
+__device__ __forceinline__ void epilogue_prefetch_row(const EpilogueParams& e, int m, int n0, int cols, int M,
+                                                      int N) {
+  if (e.beta == 0.0f || m >= M || n0 >= N) return;
+  const int n = min(cols, N - n0);
+  prefetch_l2_bulk(e.c_in + (size_t)m * (size_t)e.ldc_in + n0, (uint32_t)((n + 7) & ~7) * 2u);
+}
+
 struct GemmParams {
   int32_t M, N, K;
   int32_t num_m_blk, num_n_blk, num_k_blk;
@@ -401,6 +412,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, p, mb, nb);
+      if constexpr (EPI) epilogue_prefetch_row(p.epi, mb * kBM + q * kEpiRowsPerWarp + (int)lane, nb * BN, BN, p.M, p.N);
       const bool got = mbar_wait(accf_bar(acc), acc_phase, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, got)) {
         if (lane == 0) raise_status(p, abort_flag, kDevTimeoutEpilogue);

@@ -277,6 +277,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     int sbuf = 0;
     for (int w = pair; w < p.num_work; w += num_pairs) {
       const WorkItem wk = work_item(w, p);
+      if constexpr (EPI) {
+        if (wk.part < 0 || wk.part == p.sk_parts - 1) {
+          epilogue_prefetch_row(p.epi, wk.mb * kPairBM + (int)rank * kBM + q * kEpiRowsPerWarp + (int)lane,
+                                wk.nb * BN, BN, p.M, p.N);
+        }
+      }
       const bool got = mbar_wait(accf_bar(acc), acc_phase, p.timeout_ns, abort_flag);
       // All four epilogue warps take the same decision (they meet at named
       // barriers below, so none may leave the loop alone).

@@ -77,6 +77,12 @@ struct SkinnySmemPlan {
   __host__ __device__ static constexpr int cstage_bytes(int S) {
     return S > 1 ? MPAD * (kSkinnyBN / S) * 4 : 4 * MPAD * 32 * 4;  // room for fp32 D
   }
+  // Fused-epilogue variant only: the tile's block of C_in, [MPAD][128] bf16,
+  // in its own region after the barriers, loaded while the K loop runs.
+  static constexpr int kCinTileBytes = MPAD * kSkinnyBN * 2;
+  static constexpr int kOffCinTile = (kBytes + 127) & ~127;
+  static constexpr int kAllocBytesEpi = kOffCinTile + kCinTileBytes + 1024;
+  static_assert(kAllocBytesEpi <= 232448, "fused-epilogue shared memory plan exceeds 227 KiB");
   __host__ __device__ static constexpr bool fits(int S) { return cstage_off(S) + cstage_bytes(S) <= kRingBytes; }
   // Largest power-of-two split count (<= 8) whose reduction scratch fits.
   __host__ __device__ static constexpr int max_splits() { return fits(8) ? 8 : fits(4) ? 4 : fits(2) ? 2 : 1; }
@@ -84,17 +90,12 @@ struct SkinnySmemPlan {
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 256, "UMMA N must be 16..256 in steps of 16");
 };
 
-// Fused epilogue for element [m, n] of D (one fp32 accumulator value x):
-// same operations and order as epilogue_row32.
-__device__ __forceinline__ float skinny_epi(float x, const EpilogueParams& e, int m, int n, int M, int N,
-                                            float bias_n) {
+// Fused epilogue for element [m, n] of D given its C_in value (0 when not
+// read): same operations and order as epilogue_row32.
+__device__ __forceinline__ float skinny_epi(float x, const EpilogueParams& e, float bias_n, float cin) {
   x = __fmul_rn(e.alpha, x);
   x = __fadd_rn(x, bias_n);
-  float c = 0.0f;
-  if (e.beta != 0.0f && m < M && n < N) {
-    c = bf16_bits_to_f32(ld_global_u16(e.c_in + (size_t)m * (size_t)e.ldc_in + n));
-  }
-  return __fadd_rn(x, __fmul_rn(e.beta, c));
+  return __fadd_rn(x, __fmul_rn(e.beta, cin));
 }
 
 // Writes D element (one fp32 value) into a staging tile as bf16 or fp32.
@@ -301,6 +302,46 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (i + 1 < kN) tmem_chunk_wait(v[(i + 1) & 1]);
     }
   };
+  const int S = p.splits;
+  const int R = kSkinnyBN / S;
+  // Fused epilogue: while the K loop runs, the epilogue warps copy the C_in
+  // block this CTA will read (every row m < M; the whole tile's 128 columns,
+  // or with a split the R owned ones) into its shared-memory region,
+  // [MPAD][128] bf16, with 16-byte loads.
+  const uint32_t cin_tile = base + (uint32_t)Plan::kOffCinTile;
+  const bool use_c = EPI && p.epi.active && p.epi.beta != 0.0f;
+  if constexpr (EPI) {
+    if (epi && use_c) {
+      const int c_lo = S == 1 ? 0 : (int)rank * R;  // first tile column read
+      const int groups = (S == 1 ? kSkinnyBN : R) / 8;
+      for (int i = (int)threadIdx.x - 64; i < MPAD * groups; i += kEpiWarps * 32) {
+        const int m = i / groups, col = c_lo + (i - m * groups) * 8;
+        const int nn = n0 + col;
+        uint4 w = make_uint4(0u, 0u, 0u, 0u);
+        if (m < p.M) {
+          const __nv_bfloat16* src = p.epi.c_in + (size_t)m * (size_t)p.epi.ldc_in + nn;
+          if (nn + 8 <= p.N) {
+            w = ld_global_v4_u32(src);
+          } else {
+            uint32_t h[8];
+#pragma unroll
+            for (int e2 = 0; e2 < 8; ++e2) h[e2] = nn + e2 < p.N ? ld_global_u16(src + e2) : 0u;
+            w = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+          }
+        }
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cin_tile + (uint32_t)((m * kSkinnyBN + col) * 2)),
+                     "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w)
+                     : "memory");
+      }
+      named_bar_sync(1, kEpiWarps * 32);  // the block is in before any warp reads it
+    }
+  }
+  // C_in[m, n0 + col] from the staged block.
+  auto cin_at = [&](int m, int col) -> float {
+    uint16_t hb;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hb) : "r"(cin_tile + (uint32_t)((m * kSkinnyBN + col) * 2)));
+    return bf16_bits_to_f32(hb);
+  };
   bool have_acc = false;
   if (epi) {
     const bool got = mbar_wait(accf_bar, 0u, p.timeout_ns, abort_flag);
@@ -308,7 +349,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (!have_acc && lane == 0) skinny_raise(p, abort_flag, kDevTimeoutEpilogue);
     tc_fence_after();
   }
-  const int S = p.splits;
 
   if (S == 1) {
     // Whole tile here: each warp rounds its 32 rows and stores them as one
@@ -326,7 +366,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int j = 0; j < kChunk; ++j) {
           float x = __uint_as_float(v[j]);
           if constexpr (EPI) {
-            if (p.epi.active) x = skinny_epi(x, p.epi, c + j, n, p.M, p.N, bias_n);
+            if (p.epi.active) {
+              x = skinny_epi(x, p.epi, bias_n, use_c ? cin_at(c + j, row) : 0.0f);
+            }
           }
           skinny_stage(stage_buf, (c + j) * 32 + (int)lane, x, f32);
         }
@@ -357,7 +399,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   //      shared memory is still a copy's source or destination.  Each CTA
   //      arrives once its incoming blocks are in and rounds, stores its rows
   //      before waiting.
-  const int R = kSkinnyBN / S;
   const uint32_t blk = (uint32_t)Plan::block_bytes(S);
   const uint32_t recv_base = base;                                   // [S][R][kPitch]
   const uint32_t send_base = base + (uint32_t)Plan::recv_bytes(S);   // [S-1][R][kPitch]
@@ -390,6 +431,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     bulk_copy_to_cluster(mapa_shared(recv_base + (uint32_t)rank * blk, (uint32_t)o), send_base + lane * blk, blk,
                          mapa_shared(red_bar, (uint32_t)o));
   }
+  // Owner phase mapping: the 128 epilogue threads split the owned block,
+  // thread t takes row t % R and CPT consecutive columns.  With a fused
+  // epilogue its bias and C_in values are loaded now, while the partials
+  // are still arriving.
+  constexpr int kMinCpt = 4;
+  constexpr int kMaxCpt = MPAD / 2 > kMinCpt ? MPAD / 2 : kMinCpt;  // R <= 64
+  const int cpt = max(kMinCpt, MPAD * R / (kEpiWarps * 32));
+  const int t = (int)threadIdx.x - 64;
+  const bool owner_thread = epi && t >= 0 && t < R * (MPAD / cpt);
+  const int r = owner_thread ? t % R : 0;
+  const int c0 = owner_thread ? (t / R) * cpt : 0;
+  const int n = n0 + (int)rank * R + r;  // column n of D
+  float bias_n = 0.0f;
+  if constexpr (EPI) {
+    if (owner_thread && p.epi.active && p.epi.bias != nullptr && n < p.N) {
+      bias_n = bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p.epi.bias) + n));
+    }
+  }
   bool go = false;
   if (epi) {
     bool in = false;
@@ -406,51 +465,41 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   cluster_arrive();  // #2
   if (epi && go) {
     // Sum the S partials of the owned rows in split order (deterministic),
-    // apply the epilogue, stage D[m, n0 + rank*R + r] as [MPAD][R].  The 128
-    // epilogue threads split the block: thread t takes row t % R and CPT
-    // consecutive columns.
-    constexpr int kMinCpt = 4;
-    const int cpt = max(kMinCpt, MPAD * R / (kEpiWarps * 32));
-    const int groups = MPAD / cpt;
-    const int t = (int)threadIdx.x - 64;
+    // apply the epilogue, stage D[m, n0 + rank*R + r] as [MPAD][R].
     const bool f32 = EPI && p.epi.out_f32 != 0;
-    if (t < R * groups) {
-      const int r = t % R;
-      const int c0 = (t / R) * cpt;
-      const int n = n0 + (int)rank * R + r;  // column n of D
-      float bias_n = 0.0f;
-      if (EPI && p.epi.active && p.epi.bias != nullptr && n < p.N) {
-        bias_n = bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p.epi.bias) + n));
-      }
-#pragma unroll 2
-      for (int c = c0; c < c0 + cpt; c += 4) {
-        // All S loads first (independent), then the sum in split order.
-        float4 x[kMaxSplits];
+    if (owner_thread) {
 #pragma unroll
-        for (int sp = 0; sp < kMaxSplits; ++sp) {
-          if (sp < S) {
-            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                         : "=f"(x[sp].x), "=f"(x[sp].y), "=f"(x[sp].z), "=f"(x[sp].w)
-                         : "r"(recv_base + (uint32_t)sp * blk + (uint32_t)((r * Plan::kPitch + c) * 4)));
-          }
-        }
-        float a[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int cc = 0; cc < kMaxCpt; cc += 4) {
+        if (cc < cpt) {
+          const int c = c0 + cc;
+          // All S loads first (independent), then the sum in split order.
+          float4 x[kMaxSplits];
 #pragma unroll
-        for (int sp = 0; sp < kMaxSplits; ++sp) {
-          if (sp < S) {
-            a[0] += x[sp].x;
-            a[1] += x[sp].y;
-            a[2] += x[sp].z;
-            a[3] += x[sp].w;
+          for (int sp = 0; sp < kMaxSplits; ++sp) {
+            if (sp < S) {
+              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                           : "=f"(x[sp].x), "=f"(x[sp].y), "=f"(x[sp].z), "=f"(x[sp].w)
+                           : "r"(recv_base + (uint32_t)sp * blk + (uint32_t)((r * Plan::kPitch + c) * 4)));
+            }
           }
-        }
+          float a[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float x = a[j];
-          if constexpr (EPI) {
-            if (p.epi.active) x = skinny_epi(x, p.epi, c + j, n, p.M, p.N, bias_n);
+          for (int sp = 0; sp < kMaxSplits; ++sp) {
+            if (sp < S) {
+              a[0] += x[sp].x;
+              a[1] += x[sp].y;
+              a[2] += x[sp].z;
+              a[3] += x[sp].w;
+            }
           }
-          skinny_stage(cstage, (c + j) * R + r, x, f32);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            float v = a[jj];
+            if constexpr (EPI) {
+              if (p.epi.active) v = skinny_epi(v, p.epi, bias_n, use_c ? cin_at(c + jj, (int)rank * R + r) : 0.0f);
+            }
+            skinny_stage(cstage, (c + jj) * R + r, v, f32);
+          }
         }
       }
     }

@@ -181,6 +181,11 @@ __device__ __forceinline__ uint32_t ld_global_u16(const void* p) {
   asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p));
   return v;
 }
+// Ask L2 to fetch [p, p + bytes) from HBM ahead of use (bytes a multiple of
+// 16, p 16-byte aligned); no data reaches this thread.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void st_global_v4(float* p, float a, float b, float c, float d) {
   asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
