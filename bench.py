@@ -467,8 +467,9 @@ def run_rowshard(args) -> int:
         # All ranks must issue the same number of collectives: agree on the
         # step time (max over ranks) before deriving the step counts from it.
         one = max(_max_over_ranks(e0.elapsed_time(e1), world), 1e-3)
+        # (--steps is ignored here: each mode runs for about one second.)
         warm = max(args.warmup, int(1500.0 / one) + 1)
-        steps = max(args.steps, int(1000.0 / one) + 1)
+        steps = max(3, int(1000.0 / one) + 1)
         for _ in range(warm):
             step(bcast)
         torch.cuda.synchronize()
@@ -482,10 +483,12 @@ def run_rowshard(args) -> int:
         res[name] = _max_over_ranks(e0.elapsed_time(e1) / steps, world)
     b200_gemm.check_status()
     # Optional C all-gather (every rank ends with the whole [M, N] C), timed
-    # separately as the BASELINE asks.
-    gather_ms = None
+    # separately as the BASELINE asks; then the whole step with the gather:
+    # broadcast + GEMM + NCCL all-gather, against broadcast + the GEMM with the
+    # all-gather fused into its epilogue (b200_gemm_bf16_allgather).
+    gather_ms = unfused_ms = fused_ms = None
     if world > 1:
-        from b200_gemm.dist import gather_rows
+        from b200_gemm.dist import GatheredC, gather_rows, row_sharded_gemm_gather
         full = gather_rows(c, M)
         torch.cuda.synchronize()
         _barrier(world)
@@ -499,6 +502,40 @@ def run_rowshard(args) -> int:
         _barrier(world)
         gather_ms = _max_over_ranks(e0.elapsed_time(e1) / reps, world)
         del full
+        gbuf = GatheredC(M, N)
+
+        def unfused():
+            step(True)
+            return gather_rows(c, M)
+
+        def fused():
+            return row_sharded_gemm_gather(a, b, gathered=gbuf, M=M, b_layout="nk")
+
+        times = {}
+        for name, fn in (("unfused", unfused), ("fused", fused)):
+            fn()
+            torch.cuda.synchronize()
+            _barrier(world)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            one = max(_max_over_ranks(e0.elapsed_time(e1), world), 1e-3)
+            n_warm, n = int(500.0 / one) + 1, int(1000.0 / one) + 2
+            for _ in range(n_warm):
+                fn()
+            torch.cuda.synchronize()
+            _barrier(world)
+            e0.record()
+            for _ in range(n):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            _barrier(world)
+            times[name] = _max_over_ranks(e0.elapsed_time(e1) / n, world)
+        unfused_ms, fused_ms = times["unfused"], times["fused"]
+        b200_gemm.check_status()
+        gbuf.close()
     flops = 2.0 * M * N * K
     if rank == 0:
         print(json.dumps({
@@ -507,6 +544,8 @@ def run_rowshard(args) -> int:
             "ms_per_step": round(res["broadcast_plus_gemm"], 4), "gemm_only_ms": round(res["gemm_only"], 4),
             "gemm_only_tflops": round(flops / (res["gemm_only"] / 1e3) / 1e12, 2), "scaling": "strong",
             "c_allgather_ms": round(gather_ms, 3) if gather_ms is not None else None,
+            "step_with_allgather_ms": {"gemm_then_nccl_allgather": round(unfused_ms, 4) if unfused_ms else None,
+                                       "gemm_with_fused_allgather": round(fused_ms, 4) if fused_ms else None},
             "config": {"M": M, "N": N, "K": K, "b_layout": "nk", "chunks": args.chunks,
                        "panel_rows": e - s, "timing": "device, max over ranks"}}), flush=True)
     if world > 1:

@@ -24,6 +24,8 @@ B200_ERR_SCRATCH_LIMIT = 8
 B200_B_NK = 0
 B200_B_KN = 1
 
+B200_IPC_HANDLE_BYTES = 64
+
 B200_DTYPE_BF16 = 0
 B200_DTYPE_F32 = 1
 
@@ -52,6 +54,14 @@ _SIGNATURES = {
                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int, ctypes.POINTER(Epilogue), ctypes.c_void_p]),
+    "b200_gemm_bf16_allgather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
+                                                ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]),
+    "b200_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+    "b200_ipc_free": (ctypes.c_int, [ctypes.c_void_p]),
+    "b200_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "b200_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
     "b200_gemm_bf16_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                               ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

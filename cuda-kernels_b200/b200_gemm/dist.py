@@ -152,6 +152,118 @@ def _comm_stream(device) -> "torch.cuda.Stream":
     return _COMM_STREAMS[key]
 
 
+class _DevBuf:
+    """__cuda_array_interface__ view of raw device memory (int16 words; viewed as bf16 by the caller)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class GatheredC:
+    """Gathered-C buffers for the fused GEMM + all-gather: every rank owns a
+    [M, ldc] bf16 buffer (allocated with b200_ipc_alloc) and maps every other
+    rank's into its process (b200_ipc_open), so the gathering kernel can store
+    its C tiles straight into all of them over NVLink.  Collective: every rank
+    of `group` constructs it (and closes it) in the same order."""
+
+    def __init__(self, M: int, N: int, group=None, device=None):
+        import ctypes
+        from . import _lib
+        self._lib = _lib.load()
+        self.M, self.N = M, N
+        self.ldc = (N + 7) // 8 * 8
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the gathering GEMM stores to at most 8 ranks")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        nbytes = max(M * self.ldc * 2, 16)
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _lib.B200_IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            rc = self._lib.b200_ipc_alloc(nbytes, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p))
+        if rc != _lib.B200_OK:
+            raise _lib.B200GemmError(rc, "b200_ipc_alloc")
+        self._own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.ptrs = []
+        self._opened = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.ptrs.append(self._own)
+                    continue
+                hb = (ctypes.c_ubyte * _lib.B200_IPC_HANDLE_BYTES).from_buffer_copy(h)
+                peer = ctypes.c_void_p()
+                rc = self._lib.b200_ipc_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(peer))
+                if rc != _lib.B200_OK:
+                    raise _lib.B200GemmError(rc, f"b200_ipc_open(rank {r})")
+                self.ptrs.append(peer.value)
+                self._opened.append(peer.value)
+        full = torch.as_tensor(_DevBuf(self._own, (M, self.ldc)), device=self.device).view(torch.bfloat16)
+        self.local = full[:, :N]  # this rank's gathered C
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then (after every rank has) free this rank's."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self._lib.b200_ipc_close(p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.local = None
+        with torch.cuda.device(self.device):
+            self._lib.b200_ipc_free(self._own)
+        self._own = None
+
+
+def row_sharded_gemm_gather(a_local: torch.Tensor, b: torch.Tensor, *, gathered: GatheredC, M: int,
+                            b_layout: str = "nk", src: int = 0, group=None, broadcast: bool = True) -> torch.Tensor:
+    """One row-sharded GEMM step with the C all-gather fused into the GEMM
+    (b200_gemm_bf16_allgather): every rank's epilogue stores its C tiles into
+    every rank's gathered C.  Returns this rank's full [M, N] C.
+
+    Ordering: before the kernel, the ranks meet in the B broadcast (or a
+    barrier collective when broadcast=False), so no rank is still reading the
+    previous step's gathered C when the others start writing it; after the
+    kernel, a barrier collective on the same stream makes the result complete
+    on every rank."""
+    import ctypes
+    from . import _lib
+    lib = _lib.load()
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    start, stop = shard_rows(M, world, rank)
+    if a_local.shape[0] != stop - start:
+        raise ValueError(f"rank {rank}: A panel has {a_local.shape[0]} rows, expected {stop - start}")
+    K = a_local.shape[1]
+    N = b.shape[0] if b_layout == "nk" else b.shape[1]
+    if gathered.M != M or gathered.N != N:
+        raise ValueError("gathered-C buffers have another shape")
+    dev = a_local.device
+    token = torch.zeros(1, device=dev)
+    if broadcast:
+        broadcast_b(b, src, group)
+    else:
+        dist.all_reduce(token, group=group)
+    outs = (ctypes.c_void_p * world)(*gathered.ptrs)
+    s = torch.cuda.current_stream(dev)
+    rc = lib.b200_gemm_bf16_allgather(ctypes.c_void_p(a_local.data_ptr()), ctypes.c_void_p(b.data_ptr()), outs, world,
+                                      stop - start, N, K, max(a_local.stride(0), 1), max(b.stride(0), 1),
+                                      gathered.ldc, start, M, _lib.B200_B_NK if b_layout == "nk" else _lib.B200_B_KN,
+                                      ctypes.c_void_p(s.cuda_stream))
+    if rc != _lib.B200_OK:
+        raise _lib.B200GemmError(rc, "b200_gemm_bf16_allgather")
+    dist.all_reduce(token, group=group)  # every rank's stores are complete after this
+    return gathered.local
+
+
 def gather_rows(c_local: torch.Tensor, M: int, group=None) -> torch.Tensor:
     """All-gather the row panels of C into the full [M, N] matrix on every rank."""
     world = dist.get_world_size(group)

@@ -177,6 +177,8 @@ int init_device(int dev, DeviceState& st) {
       {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false>, wide_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, true>, wide_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, true>, wide_smem},
+      {(const void*)b200::gemm_bf16_pair_gather_kernel<false>, pair_smem},
+      {(const void*)b200::gemm_bf16_pair_gather_kernel<true>, pair_smem},
   };
   for (const KernelSmem& k : kernels) {
     if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
@@ -364,9 +366,11 @@ namespace {
 
 // `epi` == nullptr: plain GEMM, C = bf16(A op(B)).  Otherwise a validated
 // fused epilogue (see b200_gemm_bf16_ex); C is then D, of its element type.
+// `outs` != nullptr: the gathering GEMM (b200_gemm_bf16_allgather): CTA-pair
+// 256 x 256 tiles, every tile stored through each of outs->m[0 .. n_out).
 int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
               int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes, void* stream_,
-              const b200::EpilogueParams* epi_in = nullptr) {
+              const b200::EpilogueParams* epi_in = nullptr, const b200::OutMaps* outs = nullptr, int n_out = 1) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
   if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
   const int64_t kLim = 0x7fffffffLL;
@@ -398,7 +402,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   // M <= 128: swap-AB split-K kernel (HBM-bound shapes).  Larger M: CTA pairs
   // on 256-row tiles.  (The single-CTA 128-row kernel remains for callers
   // that force it with b200_gemm_set_kernel.)
-  const int force = g_force_kernel.load(std::memory_order_relaxed);
+  const int force = outs != nullptr ? kForcePair : g_force_kernel.load(std::memory_order_relaxed);
   if (force == kForceSkinny && M > 128) return B200_ERR_INVALID_ARG;
   if (force == kForceSkinny || (force == kForceAuto && M <= 128)) {
     if (M <= 16) return launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
@@ -432,7 +436,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   // A fused epilogue does more work per tile (C_in loads, fp32 stores); the
   // wide tile's single TMEM accumulator would expose it, the 256-column
   // tiles' double-buffered accumulators hide it behind the next tile.
-  const bool fused_epi = epi.active || epi.out_f32;
+  const bool fused_epi = epi.active || epi.out_f32 || outs != nullptr;
   const bool use_wide = use_pair && !use_split && !fused_epi &&
                         m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= max_pairs &&
                         wave_eff(kPairWideBN) >= 0.97 * wave_eff(kPairBN);
@@ -471,6 +475,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   p.timeout_ns = st->timeout_ns;
   p.status = st->status_ptr;
   p.epi = epi;
+  p.num_out = 1;
 
   if (!use_pair) {
     p.sk_first = p.num_work = p.num_tiles;
@@ -544,6 +549,13 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
        {b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false>,
         b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, true>}}};
   const bool fused = epi.active || epi.out_f32;
+  if (outs != nullptr) {
+    p.num_out = n_out;
+    const cudaError_t e =
+        p.b_mn_major ? cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_gather_kernel<true>, tmA, tmB, *outs, p)
+                     : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_gather_kernel<false>, tmA, tmB, *outs, p);
+    return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  }
   const PairKernel kern = kPair[use_wide ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
@@ -588,6 +600,85 @@ extern "C" B200_API int b200_gemm_bf16_ex(const void* A, const void* B, void* D,
   }
   e.active = (e.alpha != 1.0f || e.beta != 0.0f || e.bias != nullptr) ? 1u : 0u;
   return gemm_impl(A, B, D, M, N, K, lda, ldb, ldd, b_layout, nullptr, 0, stream, &e);
+}
+
+extern "C" B200_API int b200_gemm_bf16_allgather(const void* A, const void* B, void* const* outputs,
+                                                 int num_outputs, int64_t M_local, int64_t N, int64_t K, int64_t lda,
+                                                 int64_t ldb, int64_t ldc, int64_t row0, int64_t M_total,
+                                                 int b_layout, void* stream) {
+  if (outputs == nullptr || num_outputs < 1 || num_outputs > b200::kMaxOutMaps) return B200_ERR_INVALID_ARG;
+  if (M_local < 0 || N < 0 || K < 0 || row0 < 0 || M_total < 0 || row0 + M_local > M_total) {
+    return B200_ERR_INVALID_ARG;
+  }
+  if (M_local == 0 || N == 0) return B200_OK;
+  if (K == 0) return B200_ERR_INVALID_ARG;  // no kernel for an empty reduction here
+  if (ldc < N) return B200_ERR_INVALID_ARG;
+  if ((ldc % 8) != 0) return B200_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  b200::OutMaps outs{};
+  for (int i = 0; i < num_outputs; ++i) {
+    if (outputs[i] == nullptr || !aligned16(outputs[i])) return B200_ERR_ALIGNMENT;
+    // Every output must be device memory this process can address (a local
+    // buffer or a peer's buffer opened with b200_ipc_open).
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, outputs[i]) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return B200_ERR_INVALID_ARG;
+    }
+    // This rank's rows of rank i's gathered C: a [M_local, N] view starting
+    // at row row0, so that TMA clips the last tile at M_local.
+    const char* base = static_cast<const char*>(outputs[i]) + (size_t)row0 * (size_t)ldc * 2;
+    if ((rc = encode_2d(&outs.m[i], base, (uint64_t)N, (uint64_t)M_local, (uint64_t)ldc, b200::kEpiCols,
+                        b200::kEpiRowsPerWarp, false)) != B200_OK)
+      return rc;
+  }
+  void* C0 = static_cast<char*>(outputs[0]) + (size_t)row0 * (size_t)ldc * 2;
+  return gemm_impl(A, B, C0, M_local, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream, nullptr, &outs,
+                   num_outputs);
+}
+
+extern "C" B200_API int b200_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+  if (dev_ptr == nullptr || handle == nullptr || bytes == 0) return B200_ERR_INVALID_ARG;
+  *dev_ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return B200_ERR_CUDA;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == B200_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return B200_OK;
+}
+
+extern "C" B200_API int b200_ipc_free(void* dev_ptr) {
+  return cudaFree(dev_ptr) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+extern "C" B200_API int b200_ipc_open(const void* handle, void** dev_ptr) {
+  if (dev_ptr == nullptr || handle == nullptr) return B200_ERR_INVALID_ARG;
+  *dev_ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_CUDA;
+  }
+  *dev_ptr = p;
+  return B200_OK;
+}
+
+extern "C" B200_API int b200_ipc_close(void* dev_ptr) {
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
 extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {

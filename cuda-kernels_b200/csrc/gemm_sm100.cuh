@@ -172,6 +172,15 @@ struct GemmParams {
   float* workspace;      // [split tiles][sk_parts-1][2 CTAs][BN/4][128][4] fp32
   uint64_t* flags;       // [split tiles][sk_parts-1][2 CTAs]
   EpilogueParams epi;
+  int32_t num_out;       // output tensor maps each C tile is stored to (1, or one per rank when gathering)
+};
+
+// Output tensor maps of the gathering GEMM (b200_gemm_bf16_allgather): the
+// rows this rank computes, in every rank's gathered C, each mapped in this
+// process (peer buffers through CUDA IPC).
+constexpr int kMaxOutMaps = 8;
+struct OutMaps {
+  CUtensorMap m[kMaxOutMaps];
 };
 
 template <int BN, int STAGES>

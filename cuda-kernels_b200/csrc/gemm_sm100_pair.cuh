@@ -68,13 +68,11 @@ struct PairSmemPlan {
   static_assert(kAccN * BN <= kTmemCols, "accumulators must fit in TMEM");
 };
 
-template <int BN, int STAGES, bool B_MN, bool EPI = false>
-__global__ void __launch_bounds__(kNumThreads, 1)
-    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                          const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-#if B200_NO_SM100A_FEATURES
-  if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
-#else
+// Kernel body, shared by the plain/fused kernel (one output map) and the
+// gathering kernel (one output map per rank: every C tile is stored to each).
+template <int BN, int STAGES, bool B_MN, bool EPI>
+__device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
+                                               const CUtensorMap* outs, const int n_out, const GemmParams& p) {
   using Plan = PairSmemPlan<BN, STAGES>;
   constexpr int kNSub = Plan::kNSub;
   constexpr int kAccN = Plan::kAccN;
@@ -118,7 +116,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    tma_prefetch_desc(&tmC);
+    for (int i = 0; i < n_out; ++i) tma_prefetch_desc(outs + i);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(const_cast<uint32_t*>(tmem_holder)), kTmemCols);
@@ -373,8 +371,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf0, n0, row);
-          if (f32) tma_store_2d(&tmC, buf1, n0 + 32, row);
+          for (int i = 0; i < n_out; ++i) {
+            tma_store_2d(outs + i, buf0, n0, row);
+            if (f32) tma_store_2d(outs + i, buf1, n0 + 32, row);
+          }
           bulk_commit_group();
         }
         sbuf ^= 1;
@@ -390,7 +390,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         acc_phase ^= 1u;
       }
     }
-    if (lane == 0) bulk_wait_group_read<0>();  // smem reads done; the global writes complete with the grid
+    if (lane == 0) {
+      if (n_out > 1) {
+        // Gathering: the stores into other GPUs' memory are complete and
+        // visible system-wide before this CTA exits.
+        bulk_wait_group<0>();
+        __threadfence_system();
+      } else {
+        bulk_wait_group_read<0>();  // smem reads done; the global writes complete with the grid
+      }
+    }
     __syncwarp();
   }
 
@@ -401,7 +410,32 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
-#endif  // B200_NO_SM100A_FEATURES
+}
+
+template <int BN, int STAGES, bool B_MN, bool EPI = false>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmC, const __grid_constant__ GemmParams p) {
+#if B200_NO_SM100A_FEATURES
+  if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
+#else
+  pair_gemm_body<BN, STAGES, B_MN, EPI>(tmA, tmB, &tmC, 1, p);
+#endif
+}
+
+// Row-sharded GEMM with the C all-gather fused in: 256 x 256 pair tiles
+// (double-buffered accumulators keep the MMAs running while the epilogue
+// stores each tile p.num_out times), every tile stored to each rank's
+// gathered C through `outs`.
+template <bool B_MN>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_bf16_pair_gather_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                 const __grid_constant__ OutMaps outs, const __grid_constant__ GemmParams p) {
+#if B200_NO_SM100A_FEATURES
+  if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
+#else
+  pair_gemm_body<256, 6, B_MN, false>(tmA, tmB, outs.m, p.num_out, p);
+#endif
 }
 
 }  // namespace b200

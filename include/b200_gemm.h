@@ -96,6 +96,37 @@ B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M,
                                int64_t ldb, int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/*
+ * Row-sharded GEMM with the C all-gather fused in.  This rank computes rows
+ * [row0, row0 + M_local) of C = A op(B) (A_local holds exactly those rows)
+ * and its epilogue stores every C tile into each of the num_outputs
+ * gathered-C buffers: outputs[r] is rank r's [M_total, ldc] bf16 C, mapped in
+ * this process (this rank's own buffer, and the peers' opened with
+ * b200_ipc_open).  Tiles leave over NVLink while later tiles are computed,
+ * so no separate all-gather pass over C is needed.  When every rank's
+ * kernel has completed (e.g. after a collective on the same stream), every
+ * buffer holds all M_total rows.  num_outputs <= 8, K >= 1; no fused
+ * epilogue, sequential K.  No reference counterpart: the reference has no
+ * multi-GPU path; this replaces GEMM + NCCL all-gather of C in the sharded
+ * driver.
+ */
+B200_API int b200_gemm_bf16_allgather(const void* A_local, const void* B, void* const* outputs, int num_outputs,
+                                      int64_t M_local, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                      int64_t row0, int64_t M_total, int b_layout, void* stream);
+
+/*
+ * CUDA IPC helpers for the gathering GEMM's buffers (one process per GPU).
+ * b200_ipc_alloc: cudaMalloc `bytes` on the current device and write its
+ * B200_IPC_HANDLE_BYTES-byte handle; b200_ipc_open: map a peer's buffer from
+ * its handle into this process (peer access enabled); b200_ipc_close /
+ * b200_ipc_free undo them.  No reference counterpart.
+ */
+#define B200_IPC_HANDLE_BYTES 64
+B200_API int b200_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+B200_API int b200_ipc_free(void* dev_ptr);
+B200_API int b200_ipc_open(const void* handle, void** dev_ptr);
+B200_API int b200_ipc_close(void* dev_ptr);
+
 /* Element type of D for b200_gemm_bf16_ex. */
 #define B200_DTYPE_BF16 0
 #define B200_DTYPE_F32 1

@@ -61,3 +61,59 @@ def test_row_sharded_gemm_nccl(tmp_path, layout, chunks):
     ref = o.gemm_bf16(bits(a), bits(b), 0 if layout == "nk" else 1)
     c32 = o.gemm_f32acc(bits(a), bits(b), 0 if layout == "nk" else 1).astype(np.float64)
     check_parity(bits(c), c32, ref, ctx=f"row-sharded x{world} {layout}")
+
+
+def _gather_worker(rank, world, port, M, N, K, layout, steps, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+    import torch.distributed as dist
+    import b200_gemm
+    from b200_gemm.dist import GatheredC, row_sharded_gemm_gather, shard_rows
+    from tests._util import uniform_bf16
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    g = None
+    try:
+        g = GatheredC(M, N)
+        s, e = shard_rows(M, world, rank)
+        outs = []
+        for step in range(steps):  # consecutive steps reuse the gathered buffers
+            a_full = uniform_bf16((M, K), 21 + step)
+            b_full = uniform_bf16((N, K) if layout == "nk" else (K, N), 31 + step)
+            a = a_full[s:e].cuda()
+            b = b_full.cuda() if rank == 0 else torch.zeros(b_full.shape, dtype=torch.bfloat16, device="cuda")
+            full = row_sharded_gemm_gather(a, b, gathered=g, M=M, b_layout=layout)
+            outs.append(full.cpu().clone())
+        torch.cuda.synchronize()
+        assert b200_gemm.check_status() == 0
+        torch.save(outs, os.path.join(result_dir, f"c{rank}.pt"))
+    finally:
+        if g is not None:
+            g.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_gemm_with_fused_allgather(tmp_path, layout):
+    """b200_gemm_bf16_allgather: every rank ends with the whole C, equal on all
+    ranks and within the parity bounds of the oracle; two steps in a row."""
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(world, 8)
+    M, N, K, steps = 2051, 1000, 520, 2  # ragged panels, N not a multiple of the tile
+    mp.spawn(_gather_worker, args=(world, _free_port(), M, N, K, layout, steps, str(tmp_path)), nprocs=world,
+             join=True)
+    from oracle import oracle as o
+    from tests._util import bits, check_parity, uniform_bf16
+    per_rank = [torch.load(os.path.join(tmp_path, f"c{r}.pt")) for r in range(world)]
+    for step in range(steps):
+        a = uniform_bf16((M, K), 21 + step)
+        b = uniform_bf16((N, K) if layout == "nk" else (K, N), 31 + step)
+        ref = o.gemm_bf16(bits(a), bits(b), 0 if layout == "nk" else 1)
+        c32 = o.gemm_f32acc(bits(a), bits(b), 0 if layout == "nk" else 1).astype(np.float64)
+        c0 = per_rank[0][step]
+        check_parity(bits(c0), c32, ref, ctx=f"gather x{world} {layout} step {step}")
+        for r in range(1, world):
+            assert torch.equal(per_rank[r][step], c0), f"rank {r} gathered a different C at step {step}"
