@@ -403,6 +403,37 @@ def run_epilogue(args) -> int:
     return 0
 
 
+def run_fp32(args) -> int:
+    """--fp32: the reference's fp32_matmul operator (M=N=K=4096, A and B fp32 row-major,
+    fp32_matmul/README.md:4-8): ours (three-way bf16 split on the tensor cores,
+    split kernels included in the time) against cuBLAS fp32 (torch.matmul, TF32 off)."""
+    import math
+    import torch
+    torch.cuda.set_device(0)
+    import b200_gemm
+    dev = torch.device("cuda", 0)
+    for (M, N, K) in [(4096, 4096, 4096), (8192, 8192, 8192), (128, 4096, 4096)]:
+        R = max(2, math.ceil(400e6 / (4 * (M * K + K * N + M * N))))
+        g = torch.Generator(device=dev).manual_seed(M + N + K)
+        A = [torch.randn((M, K), generator=g, device=dev) for _ in range(R)]
+        B = [torch.randn((K, N), generator=g, device=dev) for _ in range(R)]
+        C = [torch.empty((M, N), device=dev) for _ in range(R)]
+        torch.backends.cuda.matmul.allow_tf32 = False
+        fns = {"b200_f32": lambda i: b200_gemm.gemm_f32(A[i % R], B[i % R], out=C[i % R]),
+               "cublas_f32": lambda i: torch.matmul(A[i % R], B[i % R], out=C[i % R])}
+        t = _time_variants(fns, target_ms=args.target_ms)
+        b200_gemm.check_status()
+        flops = 2.0 * M * N * K
+        print(json.dumps({"what": "fp32_gemm", "config": {"M": M, "N": N, "K": K, "b_layout": "kn",
+                                                           "data": "normal", "dtype": "f32"},
+                          "ms": {k: round(v, 4) for k, v in t.items()},
+                          "tflops": {k: round(flops / (v / 1e3) / 1e12, 1) for k, v in t.items()},
+                          "vs_cublas": round(t["cublas_f32"] / t["b200_f32"], 3)}), flush=True)
+        del A, B, C
+        torch.cuda.empty_cache()
+    return 0
+
+
 def run_sweep(args) -> int:
     """--sweep: one JSON line per single-GPU BASELINE config (b200 and cuBLAS, same loop)."""
     import torch
@@ -595,6 +626,7 @@ def main(argv=None) -> int:
     ap.add_argument("--target-ms", type=float, default=250.0)
     ap.add_argument("--rowshard", action="store_true", help="BASELINE config 5: row-sharded 131072x8192x8192")
     ap.add_argument("--epilogue", action="store_true", help="fused epilogue vs unfused and vs cuBLAS addmm")
+    ap.add_argument("--fp32", action="store_true", help="fp32 GEMM (reference fp32_matmul) vs cuBLAS fp32")
     ap.add_argument("--rowshard-m", type=int, default=131072)
     ap.add_argument("--chunks", type=int, default=1, help="--rowshard: column chunks of B broadcast one by one")
     args = ap.parse_args(argv)
@@ -604,6 +636,8 @@ def main(argv=None) -> int:
         return run_shape(args)
     if args.epilogue:
         return run_epilogue(args)
+    if args.fp32:
+        return run_fp32(args)
     if args.sweep:
         return run_sweep(args)
     if args.warmup < 3:

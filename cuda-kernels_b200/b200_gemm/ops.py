@@ -142,6 +142,51 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "nk", out: torch.T
     return out
 
 
+def gemm_f32(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", out: torch.Tensor | None = None,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """fp32 C = A @ op(B) for fp32 A, B (the reference's fp32_matmul operator; its B is [K,N],
+    b_layout "kn"), on the bf16 tensor cores through an exact three-way bf16 split of each
+    operand (b200_gemm_f32); the split operands go to a workspace from torch's allocator."""
+    if b_layout not in _LAYOUTS:
+        raise ValueError(f"b_layout must be 'nk' or 'kn', got {b_layout!r}")
+    for name, t in (("A", a), ("B", b)):
+        if not isinstance(t, torch.Tensor) or t.dtype != torch.float32:
+            raise TypeError(f"{name} must be a float32 tensor")
+        if not t.is_cuda or t.dim() != 2 or (t.numel() > 0 and t.stride(1) != 1):
+            raise ValueError(f"{name} must be a row-major 2-D CUDA tensor")
+    if a.device != b.device:
+        raise ValueError("A and B must be on the same device")
+    M, K = a.shape
+    N, Kb = (b.shape[0], b.shape[1]) if b_layout == "nk" else (b.shape[1], b.shape[0])
+    if Kb != K:
+        raise ValueError(f"inner dimensions differ: A is {tuple(a.shape)}, B ({b_layout}) is {tuple(b.shape)}")
+    if out is None:
+        # D is written by TMA: its row pitch must be a multiple of 4 floats.
+        out = torch.empty((M, (N + 3) // 4 * 4), dtype=torch.float32, device=a.device)[:, :N]
+    elif out.dtype != torch.float32 or tuple(out.shape) != (M, N) or out.device != a.device \
+            or (out.numel() > 0 and out.stride(1) != 1):
+        raise ValueError(f"out must be a row-major float32 [{M}, {N}] tensor on the device of A")
+    lib = _lib.load()
+    layout = _LAYOUTS[b_layout]
+    with torch.cuda.device(a.device):
+        s = stream if stream is not None else torch.cuda.current_stream(a.device)
+        n = ctypes.c_size_t(0)
+        rc = lib.b200_gemm_f32_workspace_bytes(M, N, K, layout, ctypes.byref(n))
+        if rc != _lib.B200_OK:
+            raise B200GemmError(rc)
+        ws = torch.empty(n.value + 256, dtype=torch.uint8, device=a.device) if n.value else None
+        if ws is not None and stream is not None:
+            ws.record_stream(s)
+        ws_ptr = ((ws.data_ptr() + 255) // 256 * 256) if ws is not None else None
+        rc = lib.b200_gemm_f32(ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                               ctypes.c_void_p(out.data_ptr()), M, N, K, max(a.stride(0), 1), max(b.stride(0), 1),
+                               max(out.stride(0), 1), layout, ctypes.c_void_p(ws_ptr), n.value,
+                               ctypes.c_void_p(s.cuda_stream))
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc, f"fp32 M={M} N={N} K={K} b_layout={b_layout}")
+    return out
+
+
 def workspace_bytes(M: int, N: int, K: int, b_layout: str = "nk") -> int:
     """Split-K workspace (bytes) b200_gemm_bf16_ws wants for this shape on the current device."""
     n = ctypes.c_size_t(0)

@@ -65,9 +65,39 @@ torch::Tensor matmul_b200(torch::Tensor A, torch::Tensor B) { return run(A, B, B
 // B stored [K,N] row-major, C = A @ B.
 torch::Tensor matmul_b200_kn(torch::Tensor A, torch::Tensor B) { return run(A, B, B200_B_KN); }
 
+// The reference's fp32 operator (fp32_matmul/matmul.cpp:20-33): A [M,K] and
+// B [K,N] fp32 row-major, C = A @ B fp32 (N from B.size(1), as there).
+torch::Tensor matmul_b200_f32(torch::Tensor A, torch::Tensor B) {
+  for (const auto* t : {&A, &B}) {
+    if (t->scalar_type() != torch::kFloat32) bad_arg("A and B must be float32");
+    if (!t->is_cuda()) bad_arg("A and B must be CUDA tensors");
+    if (t->dim() != 2) bad_arg("A and B must be 2-D");
+    if (t->numel() != 0 && t->stride(1) != 1) bad_arg("A and B must be row-major");
+  }
+  if (A.device() != B.device()) bad_arg("A and B must be on the same device");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(1);
+  if (B.size(0) != K) bad_arg("inner dimensions differ");
+  const c10::cuda::CUDAGuard guard(A.device());
+  // C is written by TMA, whose row pitch must be a multiple of 4 floats.
+  const int64_t ldc = (N + 3) / 4 * 4;
+  auto Cbuf = torch::empty({M, ldc}, A.options());
+  auto C = Cbuf.narrow(1, 0, N);
+  size_t ws_bytes = 0;
+  int rc = b200_gemm_f32_workspace_bytes(M, N, K, B200_B_KN, &ws_bytes);
+  if (rc != B200_OK) throw std::runtime_error(std::string("b200_gemm_f32 failed: ") + b200_gemm_strerror(rc));
+  auto ws = torch::empty({(int64_t)ws_bytes + 256}, A.options().dtype(torch::kUInt8));
+  void* ws_ptr = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~uintptr_t(255));
+  rc = b200_gemm_f32(A.data_ptr<float>(), B.data_ptr<float>(), C.data_ptr<float>(), M, N, K,
+                     std::max<int64_t>(A.stride(0), 1), std::max<int64_t>(B.stride(0), 1),
+                     ldc, B200_B_KN, ws_ptr, ws_bytes, at::cuda::getCurrentCUDAStream(A.device().index()).stream());
+  if (rc != B200_OK) throw std::runtime_error(std::string("b200_gemm_f32 failed: ") + b200_gemm_strerror(rc));
+  return ldc == N ? C : C.contiguous();
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("matmul_b200", &matmul_b200, "B200 tcgen05 BF16 matmul, B given [N,K] (C = A @ B^T)");
   m.def("matmul_b200_kn", &matmul_b200_kn, "B200 tcgen05 BF16 matmul, B given [K,N] (C = A @ B)");
+  m.def("matmul_b200_f32", &matmul_b200_f32, "B200 FP32 matmul on the bf16 tensor cores (3-way split), C = A @ B");
 }

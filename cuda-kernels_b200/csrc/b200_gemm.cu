@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstdint>
@@ -21,6 +22,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
 #include "gemm_sm100_skinny.cuh"
+#include "split_f32.cuh"
 
 namespace {
 
@@ -679,6 +681,92 @@ extern "C" B200_API int b200_ipc_open(const void* handle, void** dev_ptr) {
 
 extern "C" B200_API int b200_ipc_close(void* dev_ptr) {
   return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+namespace {
+
+// Workspace layout of b200_gemm_f32: A' [M, ldk6] then B' ([N, ldk6] or
+// [6K, ldn]), bf16, each 256-byte aligned; ldk6 = 6K rounded up to 8.
+struct F32Plan {
+  int64_t ldk6, ld_b;
+  size_t a_bytes, b_bytes;
+  size_t total() const { return a_bytes + b_bytes; }
+};
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+F32Plan plan_f32(int64_t M, int64_t N, int64_t K, int b_layout) {
+  F32Plan f{};
+  f.ldk6 = (6 * K + 7) / 8 * 8;
+  f.a_bytes = round_up((size_t)M * (size_t)f.ldk6 * 2, 256);
+  if (b_layout == B200_B_NK) {
+    f.ld_b = f.ldk6;
+    f.b_bytes = round_up((size_t)N * (size_t)f.ldk6 * 2, 256);
+  } else {
+    f.ld_b = (N + 7) / 8 * 8;
+    f.b_bytes = round_up((size_t)6 * (size_t)K * (size_t)f.ld_b * 2, 256);
+  }
+  return f;
+}
+
+int launch_split(const float* src, int64_t rows, int64_t cols, int64_t ld_src, uint16_t* dst, int64_t ld_dst,
+                 int64_t seg_off, uint32_t order, cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return B200_OK;
+  const unsigned gx = (unsigned)std::min<int64_t>((cols + 255) / 256, 64);
+  const unsigned gy = (unsigned)std::min<int64_t>(rows, 8192);
+  b200::split_f32_bf16x3_kernel<<<dim3(gx, gy), 256, 0, stream>>>(src, rows, cols, ld_src, dst, ld_dst, seg_off,
+                                                                    order);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" B200_API int b200_gemm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {
+  if (bytes == nullptr || M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
+  if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
+  *bytes = (M == 0 || N == 0 || K == 0) ? 0 : plan_f32(M, N, K, b_layout).total();
+  return B200_OK;
+}
+
+extern "C" B200_API int b200_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                                      int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* workspace,
+                                      size_t workspace_bytes, void* stream_) {
+  if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
+  if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || 6 * K > 0x7fffffffLL) return B200_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return B200_OK;
+  if (C == nullptr || ldc < N) return B200_ERR_INVALID_ARG;
+  if (!aligned16(C) || (ldc % 4) != 0) return B200_ERR_ALIGNMENT;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (K == 0) {  // empty reduction: C = 0
+    DeviceState* st = nullptr;
+    const int rc = current_device_state(&st);
+    if (rc != B200_OK) return rc;
+    return cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, stream) == cudaSuccess
+               ? B200_OK
+               : B200_ERR_CUDA;
+  }
+  if (A == nullptr || B == nullptr || lda < K || ldb < (b_layout == B200_B_NK ? K : N)) return B200_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(A) & 3u) || (reinterpret_cast<uintptr_t>(B) & 3u)) return B200_ERR_ALIGNMENT;
+  const F32Plan f = plan_f32(M, N, K, b_layout);
+  if (workspace == nullptr || workspace_bytes < f.total()) return B200_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return B200_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  uint16_t* Ap = static_cast<uint16_t*>(workspace);
+  uint16_t* Bp = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) + f.a_bytes);
+  if ((rc = launch_split(A, M, K, lda, Ap, f.ldk6, K, b200::kSplitOrderA, stream)) != B200_OK) return rc;
+  if (b_layout == B200_B_NK) {
+    rc = launch_split(B, N, K, ldb, Bp, f.ld_b, K, b200::kSplitOrderB, stream);
+  } else {
+    rc = launch_split(B, K, N, ldb, Bp, f.ld_b, K * f.ld_b, b200::kSplitOrderB, stream);
+  }
+  if (rc != B200_OK) return rc;
+  b200::EpilogueParams e{};
+  e.alpha = 1.0f;
+  e.out_f32 = 1u;
+  return gemm_impl(Ap, Bp, C, M, N, 6 * K, f.ldk6, f.ld_b, ldc, b_layout, nullptr, 0, stream, &e);
 }
 
 extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {

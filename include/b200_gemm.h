@@ -127,6 +127,24 @@ B200_API int b200_ipc_free(void* dev_ptr);
 B200_API int b200_ipc_open(const void* handle, void** dev_ptr);
 B200_API int b200_ipc_close(void* dev_ptr);
 
+/*
+ * FP32 GEMM, the reference's fp32_matmul operator (fp32_matmul/matmul.cpp:3-9,
+ * MatmulFn over float; B stored [K,N] row-major there, B200_B_KN here; [N,K]
+ * also accepted): C[M,N] fp32 = A[M,K] fp32 x op(B) fp32, computed on the bf16
+ * tensor cores.  Each operand is split exactly into three bf16 parts and the
+ * six products above fp32 rounding are summed by one bf16 GEMM with K' = 6K
+ * and fp32 accumulation, written as fp32 (accuracy of an fp32 GEMM; see
+ * csrc/split_f32.cuh).  The split operands live in a caller workspace of
+ * b200_gemm_f32_workspace_bytes() bytes, 256-byte aligned.  C: 16-byte
+ * aligned, ldc a multiple of 4; A and B: 4-byte aligned, any pitch.
+ * Replaces the SIMT kernels matmul_v1..v5 (fp32_matmul/matmul.cu:18-325,
+ * launchers :342-431).
+ */
+B200_API int b200_gemm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes);
+B200_API int b200_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                           int64_t ldb, int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 /* Element type of D for b200_gemm_bf16_ex. */
 #define B200_DTYPE_BF16 0
 #define B200_DTYPE_F32 1

@@ -185,6 +185,60 @@ int oracle_gemm_bf16_f64(const uint16_t* A, const uint16_t* B, double* C, double
   return 0;
 }
 
+/*
+ * FP32 GEMM of the reference's fp32_matmul/ operator: A [M,K] fp32 row-major
+ * times B fp32, row-major [K,N] (fp32_matmul/README.md:8, b_layout 1) or
+ * [N,K] (b_layout 0), C fp32.  Restates the reference's plain kernel
+ * (fp32_matmul/matmul.cu:18-36): one fp32 accumulator per output starting at
+ * zero, k in increasing order, acc += a * b — which nvcc contracts to a fused
+ * multiply-add, restated here with fmaf.
+ */
+int oracle_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                    int64_t ldb, int b_layout, int threads) {
+  if (M < 0 || N < 0 || K < 0 || (b_layout != 0 && b_layout != 1)) return -1;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#else
+  threads = 1;
+#endif
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      float acc = 0.0f;
+      for (int64_t k = 0; k < K; ++k) {
+        acc = fmaf(A[m * lda + k], b_layout == 0 ? B[n * ldb + k] : B[k * ldb + n], acc);
+      }
+      C[m * N + n] = acc;
+    }
+  }
+  return 0;
+}
+
+/* Near-exact fp64 product of fp32 operands (and sum_k |a*b|), for error bounds. */
+int oracle_gemm_f32_f64(const float* A, const float* B, double* C, double* absC, int64_t M, int64_t N, int64_t K,
+                        int64_t lda, int64_t ldb, int b_layout, int threads) {
+  if (M < 0 || N < 0 || K < 0 || (b_layout != 0 && b_layout != 1)) return -1;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#else
+  threads = 1;
+#endif
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      double s = 0.0, sa = 0.0;
+      for (int64_t k = 0; k < K; ++k) {
+        const double p = (double)A[m * lda + k] * (double)(b_layout == 0 ? B[n * ldb + k] : B[k * ldb + n]);
+        s += p;
+        sa += fabs(p);
+      }
+      C[m * N + n] = s;
+      if (absC) absC[m * N + n] = sa;
+    }
+  }
+  return 0;
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

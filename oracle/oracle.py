@@ -41,6 +41,10 @@ def _load():
         lib.oracle_gemm_bf16_f32acc.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
         lib.oracle_gemm_bf16.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
         lib.oracle_gemm_bf16_f64.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
+        lib.oracle_gemm_f32.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
+        lib.oracle_gemm_f32_f64.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int]
+        lib.oracle_gemm_f32.restype = ctypes.c_int
+        lib.oracle_gemm_f32_f64.restype = ctypes.c_int
         lib.oracle_f32_to_bf16.argtypes = [vp, vp, i64]
         lib.oracle_bf16_to_f32.argtypes = [vp, vp, i64]
         for f in (lib.oracle_gemm_bf16_f32acc, lib.oracle_gemm_bf16, lib.oracle_gemm_bf16_f64):
@@ -106,6 +110,43 @@ def gemm_f64(a: np.ndarray, b: np.ndarray, b_layout: int = 0, threads: int = 0):
                                       max(K, 1), b.shape[1] if b.size else 1, b_layout, threads)
     if rc != 0:
         raise RuntimeError("oracle_gemm_bf16_f64 failed")
+    return c, s
+
+
+def _f32dims(a: np.ndarray, b: np.ndarray, b_layout: int):
+    M, K = a.shape
+    N = b.shape[0] if b_layout == 0 else b.shape[1]
+    Kb = b.shape[1] if b_layout == 0 else b.shape[0]
+    if Kb != K:
+        raise ValueError("inner dimensions differ")
+    return M, N, K
+
+
+def gemm_f32(a: np.ndarray, b: np.ndarray, b_layout: int = 1, threads: int = 0) -> np.ndarray:
+    """fp32 GEMM as the reference's fp32_matmul kernels compute it (one fp32 FMA chain per output,
+    k ascending; fp32_matmul/matmul.cu:18-36).  b_layout 1 = B [K,N] (the reference's), 0 = B [N,K]."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    M, N, K = _f32dims(a, b, b_layout)
+    c = np.empty((M, N), dtype=np.float32)
+    rc = _load().oracle_gemm_f32(a.ctypes.data, b.ctypes.data, c.ctypes.data, M, N, K, max(K, 1),
+                                 b.shape[1] if b.size else 1, b_layout, threads)
+    if rc != 0:
+        raise RuntimeError("oracle_gemm_f32 failed")
+    return c
+
+
+def gemm_f32_f64(a: np.ndarray, b: np.ndarray, b_layout: int = 1, threads: int = 0):
+    """(near-exact fp64 product, fp64 sum of |a*b|) of fp32 operands."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    M, N, K = _f32dims(a, b, b_layout)
+    c = np.empty((M, N), dtype=np.float64)
+    s = np.empty((M, N), dtype=np.float64)
+    rc = _load().oracle_gemm_f32_f64(a.ctypes.data, b.ctypes.data, c.ctypes.data, s.ctypes.data, M, N, K,
+                                     max(K, 1), b.shape[1] if b.size else 1, b_layout, threads)
+    if rc != 0:
+        raise RuntimeError("oracle_gemm_f32_f64 failed")
     return c, s
 
 

@@ -107,3 +107,19 @@ def test_epilogue_argument_errors_without_gpu():
     f32_alias = _lib.Epilogue(alpha=1.0, beta=1.0, c_in=0x10000, ldc_in=8, bias=None, d_dtype=1)
     assert lib.b200_gemm_bf16_ex(fake, fake, fake, 8, 8, 8, 8, 8, 8, 0, ctypes.byref(f32_alias),
                                  None) == _lib.B200_ERR_INVALID_ARG
+
+
+def test_f32_argument_errors_without_gpu():
+    from b200_gemm import _lib
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    fake = P(0x10000)
+    n = ctypes.c_size_t(0)
+    assert lib.b200_gemm_f32_workspace_bytes(64, 64, 64, 1, ctypes.byref(n)) == _lib.B200_OK
+    # 3 bf16 parts x 2 uses each: A' is M x 6K, B' is 6K x N, bf16
+    assert n.value == 64 * 384 * 2 + 384 * 64 * 2
+    assert lib.b200_gemm_f32(fake, fake, fake, -1, 8, 8, 8, 8, 8, 1, fake, 1 << 20, None) == _lib.B200_ERR_INVALID_ARG
+    assert lib.b200_gemm_f32(fake, fake, fake, 8, 8, 8, 8, 8, 8, 5, fake, 1 << 20, None) == _lib.B200_ERR_INVALID_ARG
+    assert lib.b200_gemm_f32(fake, fake, P(0x10004), 8, 8, 8, 8, 8, 8, 1, fake, 1 << 20, None) == _lib.B200_ERR_ALIGNMENT
+    assert lib.b200_gemm_f32(fake, fake, fake, 8, 8, 8, 8, 8, 8, 1, fake, 16, None) == _lib.B200_ERR_INVALID_ARG
+    assert lib.b200_gemm_f32(fake, fake, fake, 8, 8, 8, 8, 8, 8, 1, P(0x10010), 1 << 20, None) == _lib.B200_ERR_ALIGNMENT

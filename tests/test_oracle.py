@@ -40,6 +40,20 @@ def test_epilogue_known_answers():
     assert o.epilogue(acc, 0.5, 0.0, None, None, out="f32").ravel().tolist() == [0.75, 0.0, 1.5, 0.5]
 
 
+def test_f32_gemm_known_answers_and_accuracy():
+    a = np.array([[1, 2, 3], [-1, 0.5, 4]], dtype=np.float32)
+    b = np.array([[1, 2], [1, -1], [1, 0.25]], dtype=np.float32)  # [K,N]
+    assert o.gemm_f32(a, b, 1).tolist() == [[6.0, 0.75], [3.5, -1.5]]
+    assert o.gemm_f32(a, b.T.copy(), 0).tolist() == [[6.0, 0.75], [3.5, -1.5]]
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((40, 700)).astype(np.float32)
+    b = rng.standard_normal((700, 30)).astype(np.float32)
+    exact, absc = o.gemm_f32_f64(a, b, 1)
+    c = o.gemm_f32(a, b, 1).astype(np.float64)
+    # fp32 FMA chain: error below K * 2^-24 * sum|a*b| (the classical bound)
+    assert np.all(np.abs(c - exact) <= 700 * 2.0 ** -24 * absc)
+
+
 def test_tiny_known_product():
     # 2x3 @ (2x3)^T with exactly representable values.
     a = o.f32_to_bf16(np.array([[1, 2, 3], [-1, 0.5, 4]], dtype=np.float32))
