@@ -38,6 +38,10 @@ constexpr uint64_t kDefaultTimeoutNs = 4000000000ull;  // 4 s: far above any leg
 //   pair:   a CTA pair per 256 x 256 tile, 6-stage ring (everything else)
 constexpr int kBN = 256;
 constexpr int kStages = 4;
+// Small problems (a 256 x 256 pair tiling would leave most SMs idle): one CTA
+// per 128 x 64 tile, so up to one tile per SM.
+constexpr int kSmallBN = 64;
+constexpr int kSmallStages = 8;
 constexpr int kPairBN = 256;
 constexpr int kPairStages = 6;
 // Wide pair tiles (256 x 512): each CTA reuses its A rows for 512 output
@@ -160,6 +164,7 @@ int init_device(int dev, DeviceState& st) {
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_b200_status) != cudaSuccess)
     return B200_ERR_CUDA;
   constexpr int single_smem = b200::SmemPlan<kBN, kStages>::kAllocBytes;
+  constexpr int small_smem = b200::SmemPlan<kSmallBN, kSmallStages>::kAllocBytes;
   constexpr int pair_smem = b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
   constexpr int wide_smem = b200::PairSmemPlan<kPairWideBN, kPairWideStages>::kAllocBytes;
   struct KernelSmem {
@@ -171,6 +176,10 @@ int init_device(int dev, DeviceState& st) {
       {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, false>, single_smem},
       {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, true>, single_smem},
       {(const void*)b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, true>, single_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, false, false>, small_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, true, false>, small_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, false, true>, small_smem},
+      {(const void*)b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, true, true>, small_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false, false>, pair_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, true, false>, pair_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairBN, kPairStages, false, true>, pair_smem},
@@ -368,6 +377,16 @@ namespace {
 
 // `epi` == nullptr: plain GEMM, C = bf16(A op(B)).  Otherwise a validated
 // fused epilogue (see b200_gemm_bf16_ex); C is then D, of its element type.
+// M > 128 problems so small that 256 x 256 CTA-pair tiles would occupy at
+// most half of the SMs, while 128 x 64 single-CTA tiles fit in one wave:
+// the small tiles spread the work over up to 4x more SMs (1024^3: 16 pairs
+// = 32 SMs against 128 CTAs).
+inline bool use_small_tiles(const DeviceState& st, int64_t M, int64_t N) {
+  const int64_t pair_tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
+  const int64_t small_tiles = ((M + b200::kBM - 1) / b200::kBM) * ((N + kSmallBN - 1) / kSmallBN);
+  return M > b200::kBM && 4 * pair_tiles <= st.sm_count && small_tiles <= st.sm_count;
+}
+
 // `outs` != nullptr: the gathering GEMM (b200_gemm_bf16_allgather): CTA-pair
 // 256 x 256 tiles, every tile stored through each of outs->m[0 .. n_out).
 int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
@@ -402,8 +421,10 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   if (!aligned16(A) || !aligned16(B) || (lda % 8) != 0 || (ldb % 8) != 0) return B200_ERR_ALIGNMENT;
 
   // M <= 128: swap-AB split-K kernel (HBM-bound shapes).  Larger M: CTA pairs
-  // on 256-row tiles.  (The single-CTA 128-row kernel remains for callers
-  // that force it with b200_gemm_set_kernel.)
+  // on 256-row tiles, or single CTAs on 128 x 64 tiles for problems too
+  // small to occupy the GPU with pairs (use_small_tiles).  (The single-CTA
+  // 128 x 256 kernel remains for callers that force it with
+  // b200_gemm_set_kernel.)
   const int force = outs != nullptr ? kForcePair : g_force_kernel.load(std::memory_order_relaxed);
   if (force == kForceSkinny && M > 128) return B200_ERR_INVALID_ARG;
   if (force == kForceSkinny || (force == kForceAuto && M <= 128)) {
@@ -412,7 +433,8 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     if (M <= 64) return launch_skinny<64>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
     return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
   }
-  const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM);
+  const bool use_small = force == kForceAuto && use_small_tiles(*st, M, N);
+  const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM && !use_small);
   const int max_pairs = st->max_pairs;
   const int64_t m_blk_pair = (M + b200::kPairBM - 1) / b200::kPairBM;
   const int32_t k_blks = (int32_t)((K + b200::kBK - 1) / b200::kBK);
@@ -442,7 +464,10 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   const bool use_wide = use_pair && !use_split && !fused_epi &&
                         m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= max_pairs &&
                         wave_eff(kPairWideBN) >= 0.97 * wave_eff(kPairBN);
-  const uint32_t bn = !use_pair ? (uint32_t)kBN : use_wide ? (uint32_t)kPairWideBN : (uint32_t)kPairBN;
+  const uint32_t bn = use_small   ? (uint32_t)kSmallBN
+                      : !use_pair ? (uint32_t)kBN
+                      : use_wide  ? (uint32_t)kPairWideBN
+                                  : (uint32_t)kPairBN;
   // B rows (K-major) one TMA box covers: a pair CTA loads 128-column blocks.
   const uint32_t b_rows = use_pair ? 128u : bn;
 
@@ -485,17 +510,25 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     p.sk_kpp = p.num_k_blk;
     const int grid = (int)(tiles < st->sm_count ? tiles : st->sm_count);
     const bool fused = epi.active || epi.out_f32;
-    auto kern = p.b_mn_major ? (fused ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, true>
-                                      : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, false>)
-                             : (fused ? b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, true>
-                                      : b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, false>);
+    using SingleKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const b200::GemmParams);
+    static const SingleKernel kSingle[2][2][2] = {
+        {{b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, false>,
+          b200::gemm_bf16_tcgen05_kernel<kBN, kStages, false, true>},
+         {b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, false>,
+          b200::gemm_bf16_tcgen05_kernel<kBN, kStages, true, true>}},
+        {{b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, false, false>,
+          b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, false, true>},
+         {b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, true, false>,
+          b200::gemm_bf16_tcgen05_kernel<kSmallBN, kSmallStages, true, true>}}};
+    const SingleKernel kern = kSingle[use_small ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
-    cfg.dynamicSmemBytes = b200::SmemPlan<kBN, kStages>::kAllocBytes;
+    cfg.dynamicSmemBytes = use_small ? b200::SmemPlan<kSmallBN, kSmallStages>::kAllocBytes
+                                     : b200::SmemPlan<kBN, kStages>::kAllocBytes;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -777,7 +810,7 @@ extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t 
   const int rc = current_device_state(&st);
   if (rc != B200_OK) return rc;
   const int force = g_force_kernel.load(std::memory_order_relaxed);
-  const bool pair = force == kForcePair || (force == kForceAuto && M > 128);
+  const bool pair = force == kForcePair || (force == kForceAuto && M > 128 && !use_small_tiles(*st, M, N));
   if (!pair || M == 0 || N == 0 || K == 0) return B200_OK;
   const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
   const SplitPlan sp = plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st->max_pairs, kPairBN);

@@ -305,10 +305,13 @@ def _raw_gemm(a, b, c, layout, ws=None, ws_bytes=0):
 @pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1024, 1024, 8192), (640, 2560, 2056), (300, 520, 4100),
                                    (129, 257, 2060), (5000, 4096, 4096)], ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("layout", ["nk", "kn"])
-def test_split_k_tail_matches_oracle_and_is_deterministic(shape, layout):
+def test_split_k_tail_matches_oracle_and_is_deterministic(shape, layout, forced_kernel):
     """The last wave's tiles split along K across pairs (b200_gemm_bf16_ws):
     same product as without the split (both against the oracle), and two
-    calls give identical bits (partials are added in a fixed order)."""
+    calls give identical bits (partials are added in a fixed order).  The
+    pair kernel is forced: small shapes would otherwise take 128 x 64 tiles,
+    which have no split-K tail."""
+    forced_kernel("pair")
     M, N, K = shape
     ws_bytes = b200_gemm.ops.workspace_bytes(M, N, K, layout)
     assert ws_bytes > 0, "shape chosen to exercise the split-K tail"
