@@ -16,7 +16,9 @@
  *
  * This header replaces that surface with a plain C ABI: raw pointers, 64-bit
  * sizes, an explicit stream, and an integer status instead of a host assert.
- * No call allocates device memory, throws, or exits the process.
+ * No GEMM entry point allocates device memory (scratch comes from the
+ * caller's workspace or, for b200_gemm_bf16_noalloc, a static buffer); only
+ * b200_ipc_alloc, whose job it is, does.  No call throws or exits the process.
  *
  * All functions are thread-safe.  Device memory passed in must belong to the
  * device that is current on the calling thread.
