@@ -434,6 +434,40 @@ def run_fp32(args) -> int:
     return 0
 
 
+def run_attention(args) -> int:
+    """--attention: the reference's flash_attn benchmark (flash_attn/main.py:28-56,
+    README.md:9): causal bf16 attention, (batch, seq, heads, head_dim) = (1, S, 32, 128),
+    S = 512 ... 8192; ours against torch SDPA and the flash-attn package on the same GPU.
+    TFLOPS counted as the reference does for causal attention: 2 * 2 * B * H * S^2 * D / 2."""
+    import torch
+    import torch.nn.functional as F
+    torch.cuda.set_device(0)
+    import b200_gemm
+    dev = torch.device("cuda", 0)
+    try:
+        from flash_attn import flash_attn_func
+    except Exception:  # noqa: BLE001 - the comparison is optional
+        flash_attn_func = None
+    for S in (512, 1024, 2048, 4096, 8192):
+        g = torch.Generator(device=dev).manual_seed(S)
+        q, k, v = (torch.randn((1, S, 32, 128), generator=g, device=dev).bfloat16() for _ in range(3))
+        qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        out = torch.empty_like(q)
+        fns = {"b200": lambda i: b200_gemm.flash_attn(q, k, v, causal=True, out=out),
+               "torch_sdpa": lambda i: F.scaled_dot_product_attention(qt, kt, vt, is_causal=True)}
+        if flash_attn_func is not None:
+            fns["flash_attn_pkg"] = lambda i: flash_attn_func(q, k, v, causal=True)
+        t = _time_variants(fns, target_ms=args.target_ms)
+        b200_gemm.check_status()
+        flops = 2.0 * 2.0 * 32 * S * S * 128 / 2.0
+        print(json.dumps({"what": "flash_attention_causal", "config": {"batch": 1, "seq_len": S, "heads": 32,
+                                                                        "head_dim": 128, "dtype": "bf16"},
+                          "ms": {k_: round(v_, 4) for k_, v_ in t.items()},
+                          "tflops": {k_: round(flops / (v_ / 1e3) / 1e12, 1) for k_, v_ in t.items()}}),
+              flush=True)
+    return 0
+
+
 def run_sweep(args) -> int:
     """--sweep: one JSON line per single-GPU BASELINE config (b200 and cuBLAS, same loop)."""
     import torch
@@ -627,6 +661,7 @@ def main(argv=None) -> int:
     ap.add_argument("--rowshard", action="store_true", help="BASELINE config 5: row-sharded 131072x8192x8192")
     ap.add_argument("--epilogue", action="store_true", help="fused epilogue vs unfused and vs cuBLAS addmm")
     ap.add_argument("--fp32", action="store_true", help="fp32 GEMM (reference fp32_matmul) vs cuBLAS fp32")
+    ap.add_argument("--attention", action="store_true", help="causal flash attention (reference flash_attn)")
     ap.add_argument("--rowshard-m", type=int, default=131072)
     ap.add_argument("--chunks", type=int, default=1, help="--rowshard: column chunks of B broadcast one by one")
     args = ap.parse_args(argv)
@@ -638,6 +673,8 @@ def main(argv=None) -> int:
         return run_epilogue(args)
     if args.fp32:
         return run_fp32(args)
+    if args.attention:
+        return run_attention(args)
     if args.sweep:
         return run_sweep(args)
     if args.warmup < 3:

@@ -23,6 +23,7 @@
 #include "gemm_sm100_pair.cuh"
 #include "gemm_sm100_skinny.cuh"
 #include "split_f32.cuh"
+#include "attn_sm100.cuh"
 
 namespace {
 
@@ -195,6 +196,9 @@ int init_device(int dev, DeviceState& st) {
     if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
       return B200_ERR_CUDA;
   }
+  if (cudaFuncSetAttribute(b200::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           b200::AttnSmemPlan::kAllocBytes) != cudaSuccess)
+    return B200_ERR_CUDA;
   if (set_skinny_attrs<16>() != B200_OK || set_skinny_attrs<32>() != B200_OK || set_skinny_attrs<64>() != B200_OK ||
       set_skinny_attrs<128>() != B200_OK)
     return B200_ERR_CUDA;
@@ -800,6 +804,68 @@ extern "C" B200_API int b200_gemm_f32(const float* A, const float* B, float* C, 
   e.alpha = 1.0f;
   e.out_f32 = 1u;
   return gemm_impl(Ap, Bp, C, M, N, 6 * K, f.ldk6, f.ld_b, ldc, b_layout, nullptr, 0, stream, &e);
+}
+
+namespace {
+
+// 3-D bf16 tensor map {cols, rows, batch} over a [batch, rows, ld] array,
+// 128B swizzle; rows clip per batch.
+int encode_3d(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows, uint64_t batch, uint64_t ld_elems,
+              uint32_t box_cols, uint32_t box_rows, bool is_load) {
+  cuuint64_t dims[3] = {cols, rows, batch};
+  cuuint64_t strides[2] = {ld_elems * 2, ld_elems * 2 * rows};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              is_load ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
+}
+
+}  // namespace
+
+extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const void* V, void* O, int64_t batch,
+                                             int64_t seq_len, int64_t heads, int64_t head_dim, int causal,
+                                             void* stream_) {
+  if (batch < 0 || seq_len < 0 || heads < 0) return B200_ERR_INVALID_ARG;
+  if (head_dim != b200::kAttnD) return B200_ERR_INVALID_ARG;
+  if (batch == 0 || seq_len == 0 || heads == 0) return B200_OK;
+  if (batch > 65535 || heads > 65535 || seq_len > 0x7fffffffLL || heads * head_dim > 0x7fffffffLL)
+    return B200_ERR_TOO_LARGE;
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return B200_ERR_INVALID_ARG;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return B200_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != B200_OK) return rc;
+  const uint64_t cols = (uint64_t)(heads * head_dim);
+  CUtensorMap tmQ, tmK, tmV, tmO;
+  if ((rc = encode_3d(&tmQ, Q, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 128, true)) != B200_OK ||
+      (rc = encode_3d(&tmK, K, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 128, true)) != B200_OK ||
+      (rc = encode_3d(&tmV, V, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 64, true)) != B200_OK ||
+      (rc = encode_3d(&tmO, O, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 32, false)) != B200_OK)
+    return rc;
+  b200::AttnParams p{};
+  p.seq_len = (int32_t)seq_len;
+  p.heads = (int32_t)heads;
+  p.batch = (int32_t)batch;
+  p.num_q_tiles = (int32_t)((seq_len + b200::kAttnBQ - 1) / b200::kAttnBQ);
+  p.causal = causal ? 1u : 0u;
+  p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  p.timeout_ns = st->timeout_ns;
+  p.status = st->status_ptr;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)p.num_q_tiles, (unsigned)heads, (unsigned)batch);
+  cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = b200::AttnSmemPlan::kAllocBytes;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream_);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, b200::flash_attn_fwd_kernel, tmQ, tmK, tmV, tmO, p) == cudaSuccess ? B200_OK
+                                                                                                      : B200_ERR_CUDA;
 }
 
 extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {

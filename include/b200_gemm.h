@@ -147,6 +147,17 @@ B200_API int b200_gemm_f32(const float* A, const float* B, float* C, int64_t M, 
                            int64_t ldb, int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/*
+ * Flash attention forward, the reference's flash_attn operator
+ * (flash_attn/flash_attn.cpp:5-30 and :16-25, launch_fa2_tma_lazy_rescale in
+ * fa2_tma_lazy_rescale.cu): O = softmax(Q K^T / sqrt(head_dim)) V, causal or
+ * not, bf16 Q, K, V, O of shape [batch, seq_len, heads, head_dim] (contiguous,
+ * 16-byte aligned), head_dim = 128 (as the reference requires), fp32 softmax
+ * statistics and accumulation on the tcgen05 tensor cores.
+ */
+B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const void* V, void* O, int64_t batch,
+                                  int64_t seq_len, int64_t heads, int64_t head_dim, int causal, void* stream);
+
 /* Element type of D for b200_gemm_bf16_ex. */
 #define B200_DTYPE_BF16 0
 #define B200_DTYPE_F32 1

@@ -54,6 +54,20 @@ def test_f32_gemm_known_answers_and_accuracy():
     assert np.all(np.abs(c - exact) <= 700 * 2.0 ** -24 * absc)
 
 
+def test_attention_known_answers():
+    # Q = 0: every score is equal, so each row of O is the mean of the values
+    # it may see (all of them, or the prefix with a causal mask).
+    S, D = 5, 128
+    v = np.arange(S * D, dtype=np.float32).reshape(1, S, 1, D) / 64.0
+    z = o.f32_to_bf16(np.zeros((1, S, 1, D), dtype=np.float32))
+    vb = o.f32_to_bf16(v)
+    vv = o.bf16_to_f32(vb).astype(np.float64)[0, :, 0, :]
+    full = o.attention(z, z, vb, causal=False)[0, :, 0, :]
+    causal = o.attention(z, z, vb, causal=True)[0, :, 0, :]
+    assert np.allclose(full, np.broadcast_to(vv.mean(axis=0), (S, D)))
+    assert np.allclose(causal, np.cumsum(vv, axis=0) / np.arange(1, S + 1)[:, None])
+
+
 def test_tiny_known_product():
     # 2x3 @ (2x3)^T with exactly representable values.
     a = o.f32_to_bf16(np.array([[1, 2, 3], [-1, 0.5, 4]], dtype=np.float32))
