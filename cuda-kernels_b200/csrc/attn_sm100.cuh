@@ -284,20 +284,55 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (lane == 0) mbar_arrive(s_empty(s));  // S buffer s may be overwritten by S_{j+2}
       const int kv0 = j * kAttnBKV;
       const bool diag = p.causal && kv0 + kAttnBKV > qt * kAttnBQ;  // the tile crossing the diagonal
-      float mx = -INFINITY;
+      // Scale into the exp2 domain and take the row max.  Eight independent
+      // partial maxima (and sums below): one thread owns the whole row, so a
+      // single dependency chain over 128 keys would serialise on latency.
+      // Only the diagonal tile and a tile past the sequence end need masks:
+      // keys c >= lim are masked.
+      const bool masked = diag || kv0 + kAttnBKV > p.seq_len;
+      const int lim = min(p.seq_len - kv0, diag ? q_idx - kv0 + 1 : kAttnBKV);
+      float mxs[8];
 #pragma unroll
-      for (int c = 0; c < kAttnBKV; ++c) {
-        float v = x[c] * p.scale_log2;
-        const int kv = kv0 + c;
-        if (kv >= p.seq_len || (diag && kv > q_idx)) v = -INFINITY;
-        x[c] = v;
-        mx = fmaxf(mx, v);
+      for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
+      if (!masked) {
+#pragma unroll
+        for (int c = 0; c < kAttnBKV; ++c) {
+          x[c] *= p.scale_log2;
+          mxs[c & 7] = fmaxf(mxs[c & 7], x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kAttnBKV; ++c) {
+          x[c] = c < lim ? x[c] * p.scale_log2 : -INFINITY;
+          mxs[c & 7] = fmaxf(mxs[c & 7], x[c]);
+        }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       const float m_new = fmaxf(m, mx);
       // Move the reference max only when the row max grew by more than 2^8
       // (or nothing was seen yet): P stays below 2^8, and O is rescaled rarely.
       const bool move = (m == -INFINITY) ? (m_new != -INFINITY) : (m_new > m + kAttnRescaleLog2);
       const float factor = (move && m != -INFINITY) ? fast_exp2(m - m_new) : 1.0f;
+      // P and its row sum with the max the row will use from now on — all
+      // before waiting for the previous P V product, so the exponentials
+      // overlap that MMA; P is kept packed as bf16 pairs.
+      const float m_next = move ? m_new : m;
+      const float m_use = (m_next == -INFINITY) ? 0.0f : m_next;
+      float sums[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
+      uint32_t pw[kAttnBKV / 2];
+#pragma unroll
+      for (int c = 0; c < kAttnBKV; c += 2) {
+        // exp2(-inf) is +0: masked keys need no test.
+        const float e0 = fast_exp2(x[c] - m_use);
+        const float e1 = fast_exp2(x[c + 1] - m_use);
+        sums[(c >> 1) & 7] += e0 + e1;
+        __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
+        pw[c / 2] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       if (j > 0) {
         // P_{j-1} V_{j-1} done: the P buffer is free and O is stable.
         const bool prev = mbar_wait(o_done, (uint32_t)(j - 1) & 1u, p.timeout_ns, abort_flag);
@@ -324,14 +359,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         l *= factor;
         m = m_new;
       }
-      const float m_use = (m == -INFINITY) ? 0.0f : m;
-      float sum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kAttnBKV; ++c) {
-        const float e = (x[c] == -INFINITY) ? 0.0f : fast_exp2(x[c] - m_use);
-        x[c] = e;
-        sum += e;
-      }
       l += sum;
       // P row -> shared memory, bf16, 128B-swizzled K-major (keys contiguous):
       // two atoms of 64 keys, 16-byte chunk c of row r at chunk c ^ (r & 7).
@@ -340,16 +367,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t row_addr = sP + (uint32_t)(a * 16384 + row * 128);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = a * 64 + cc * 8 + 2 * e;
-            __nv_bfloat162 h = __floats2bfloat162_rn(x[c], x[c + 1]);
-            w[e] = *reinterpret_cast<uint32_t*>(&h);
-          }
+          const int w0 = a * 32 + cc * 4;
           const uint32_t dst = row_addr + (((uint32_t)cc ^ ((uint32_t)row & 7u)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                       "r"(w[3])
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(pw[w0]), "r"(pw[w0 + 1]),
+                       "r"(pw[w0 + 2]), "r"(pw[w0 + 3])
                        : "memory");
         }
       }
