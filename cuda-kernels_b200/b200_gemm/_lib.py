@@ -70,7 +70,7 @@ _SIGNATURES = {
                                      ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "b200_flash_attn_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
-                                            ctypes.c_int, ctypes.c_void_p]),
+                                            ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]),
     "b200_gemm_bf16_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                               ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

@@ -5,6 +5,8 @@
     b200_gemm/libb200_gemm.so          C-ABI library (include/b200_gemm.h), sm_100a
     bf16_matmul/b200_matmul_ext.*.so   torch extension mirroring the reference's
                                        bf16_matmul/matmul.cpp binding
+    flash_attn/b200_flash_attn_ext.so  torch extension mirroring the reference's
+                                       flash_attn/flash_attn.cpp binding
 
 Every CUDA compile targets sm_100a explicitly
 (-gencode arch=compute_100a,code=sm_100a); nothing here depends on the GPU
@@ -26,6 +28,11 @@ INCLUDE = os.path.join(REPO, "include")
 LIB_PATH = os.path.join(PKG_DIR, "libb200_gemm.so")
 EXT_DIR = os.path.join(ROOT, "bf16_matmul")
 EXT_NAME = "b200_matmul_ext"
+# Torch extensions: (name, directory, source), each linked against the C-ABI library.
+EXTENSIONS = [
+    (EXT_NAME, EXT_DIR, "matmul.cpp"),
+    ("b200_flash_attn_ext", os.path.join(ROOT, "flash_attn"), "flash_attn.cpp"),
+]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -67,36 +74,43 @@ def build_lib(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
-def ext_path() -> str | None:
-    hits = sorted(glob.glob(os.path.join(EXT_DIR, EXT_NAME + "*.so")))
+def ext_path(name: str = EXT_NAME, ext_dir: str = EXT_DIR) -> str | None:
+    hits = sorted(glob.glob(os.path.join(ext_dir, name + "*.so")))
     return hits[0] if hits else None
 
 
-def build_ext(force: bool = False, verbose: bool = False) -> str:
-    """Build the torch-extension binding (bf16_matmul/matmul.cpp) against the C-ABI library."""
-    src = os.path.join(EXT_DIR, "matmul.cpp")
-    cur = ext_path()
+def _build_one(name: str, ext_dir: str, source: str, force: bool, verbose: bool) -> str:
+    src = os.path.join(ext_dir, source)
+    cur = ext_path(name, ext_dir)
     if not force and cur is not None and not _stale(cur, [src, LIB_PATH, os.path.join(INCLUDE, "b200_gemm.h")]):
         return cur
     import torch.utils.cpp_extension as ce
 
-    build_dir = os.path.join(EXT_DIR, "_build")
+    build_dir = os.path.join(ext_dir, "_build")
     os.makedirs(build_dir, exist_ok=True)
+    rel = os.path.relpath(PKG_DIR, ext_dir)
     ce.load(
-        name=EXT_NAME,
+        name=name,
         sources=[src],
         extra_cflags=["-O3", "-std=c++17", f"-I{INCLUDE}"],
-        extra_ldflags=[f"-L{PKG_DIR}", "-lb200_gemm", f"-Wl,-rpath,{PKG_DIR}", "-Wl,-rpath,$ORIGIN/../b200_gemm"],
+        extra_ldflags=[f"-L{PKG_DIR}", "-lb200_gemm", f"-Wl,-rpath,{PKG_DIR}", f"-Wl,-rpath,$ORIGIN/{rel}"],
         build_directory=build_dir,
         with_cuda=True,
         verbose=verbose,
         is_python_module=True,
     )
-    built = os.path.join(build_dir, EXT_NAME + ".so")
-    dst = os.path.join(EXT_DIR, EXT_NAME + ".so")
+    built = os.path.join(build_dir, name + ".so")
+    dst = os.path.join(ext_dir, name + ".so")
     shutil.copyfile(built, dst)
     shutil.rmtree(build_dir, ignore_errors=True)
     return dst
+
+
+def build_ext(force: bool = False, verbose: bool = False) -> str:
+    """Build the torch-extension bindings (bf16_matmul/matmul.cpp, flash_attn/flash_attn.cpp) against the
+    C-ABI library; returns the GEMM extension's path."""
+    paths = [_build_one(n, d, s, force, verbose) for n, d, s in EXTENSIONS]
+    return paths[0]
 
 
 def main(argv: list[str]) -> int:
@@ -104,7 +118,9 @@ def main(argv: list[str]) -> int:
     verbose = "-v" in argv or "--verbose" in argv
     print(build_lib(force=force, verbose=verbose))
     if "--no-ext" not in argv:
-        print(build_ext(force=force, verbose=verbose))
+        build_ext(force=force, verbose=verbose)
+        for n, d, _ in EXTENSIONS:
+            print(ext_path(n, d))
     return 0
 
 

@@ -189,16 +189,21 @@ def gemm_f32(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", out: tor
 
 def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
                out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """O = softmax(Q K^T / sqrt(D)) V for bf16 Q, K, V of shape [batch, seq, heads, 128] (the reference's
-    flash_attn operator, flash_attn/flash_attn.cpp:16-25), through b200_flash_attn_bf16."""
+    """O = softmax(Q K^T / sqrt(D)) V (the reference's flash_attn operator, flash_attn/flash_attn.cpp:16-25),
+    through b200_flash_attn_bf16.  Q is [batch, seq, heads, 128] bf16; K and V are [batch, seq, kv_heads, 128]
+    with heads a multiple of kv_heads (grouped-query attention: query head h uses key/value head
+    h // (heads // kv_heads), as fa2_tma_lazy_rescale.cu:113-114)."""
     for name, t in (("Q", q), ("K", k), ("V", v)):
         if not isinstance(t, torch.Tensor) or t.dtype != torch.bfloat16 or not t.is_cuda or t.dim() != 4:
             raise ValueError(f"{name} must be a 4-D bfloat16 CUDA tensor [batch, seq, heads, head_dim]")
         if not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
-    if k.shape != q.shape or v.shape != q.shape or k.device != q.device or v.device != q.device:
-        raise ValueError("Q, K and V must have the same shape and device")
     B, S, H, D = q.shape
+    Hkv = k.shape[2]
+    if k.shape != (B, S, Hkv, D) or v.shape != k.shape or k.device != q.device or v.device != q.device:
+        raise ValueError("K and V must have Q's batch, seq and head_dim, the same shape, and Q's device")
+    if Hkv == 0 and H != 0 or Hkv != 0 and H % Hkv != 0:
+        raise ValueError(f"the number of query heads ({H}) must be a multiple of the key/value heads ({Hkv})")
     if out is None:
         out = torch.empty_like(q)
     elif out.shape != q.shape or out.dtype != torch.bfloat16 or not out.is_contiguous() or out.device != q.device:
@@ -208,9 +213,9 @@ def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: boo
         s = stream if stream is not None else torch.cuda.current_stream(q.device)
         rc = lib.b200_flash_attn_bf16(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
                                       ctypes.c_void_p(v.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                                      B, S, H, D, 1 if causal else 0, ctypes.c_void_p(s.cuda_stream))
+                                      B, S, H, Hkv, D, 1 if causal else 0, ctypes.c_void_p(s.cuda_stream))
     if rc != _lib.B200_OK:
-        raise B200GemmError(rc, f"flash_attn B={B} S={S} H={H} D={D}")
+        raise B200GemmError(rc, f"flash_attn B={B} S={S} H={H} Hkv={Hkv} D={D}")
     return out
 
 

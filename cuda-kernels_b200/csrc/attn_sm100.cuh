@@ -1,7 +1,10 @@
 // Flash attention forward for sm_100a (tcgen05 + TMEM + TMA), the reference's
 // flash_attn operator (flash_attn/flash_attn.cpp:5-30, fa2_tma_lazy_rescale.cu):
 // O = softmax(Q K^T / sqrt(D)) V, optionally causal, bf16 in and out, fp32
-// softmax statistics and accumulation, Q/K/V/O stored [batch, seq, heads, 128].
+// softmax statistics and accumulation, Q/O stored [batch, seq, heads, 128] and
+// K/V [batch, seq, kv_heads, 128]; query head h reads key/value head
+// h / (heads / kv_heads) (grouped-query attention, as the reference's kernel,
+// fa2_tma_lazy_rescale.cu:113-114).
 //
 // One CTA per (128 query rows, head, batch); 192 threads:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
@@ -38,6 +41,7 @@ constexpr float kAttnRescaleLog2 = 8.0f;  // lazy rescale threshold (P stays <= 
 
 struct AttnParams {
   int32_t seq_len, heads, batch;
+  int32_t group;  // heads / kv_heads: query heads per key/value head
   int32_t num_q_tiles;
   uint32_t causal;
   float scale_log2;  // log2(e) / sqrt(D): scores go straight to the exp2 domain
@@ -112,6 +116,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int kv_tiles_all = (p.seq_len + kAttnBKV - 1) / kAttnBKV;
   const int n_kv = p.causal ? min(qt + 1, kv_tiles_all) : kv_tiles_all;
   const int col0 = head * kAttnD;  // column of this head in the [seq, heads * D] view
+  const int kv_col0 = (head / p.group) * kAttnD;  // its key/value head in [seq, kv_heads * D]
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
@@ -164,7 +169,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         mbar_arrive_expect_tx(k_full(s), Plan::kTileBytes);
         for (int i = 0; i < 2; ++i) {
-          tma_load_3d(sK + s * Plan::kTileBytes + i * 16384, &tmK, k_full(s), col0 + 64 * i, j * kAttnBKV, bat,
+          tma_load_3d(sK + s * Plan::kTileBytes + i * 16384, &tmK, k_full(s), kv_col0 + 64 * i, j * kAttnBKV, bat,
                       pol_keep);
         }
         ++k_issued;
@@ -176,7 +181,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // V tile as two 64-key halves, each two 64-column atoms of [64 keys][64 d].
         for (int hk = 0; hk < 2; ++hk) {
           for (int i = 0; i < 2; ++i) {
-            tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + i * 8192, &tmV, v_full(s), col0 + 64 * i,
+            tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + i * 8192, &tmV, v_full(s), kv_col0 + 64 * i,
                         j * kAttnBKV + 64 * hk, bat, pol_keep);
           }
         }

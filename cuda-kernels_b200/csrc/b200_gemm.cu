@@ -826,10 +826,11 @@ int encode_3d(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows, u
 }  // namespace
 
 extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const void* V, void* O, int64_t batch,
-                                             int64_t seq_len, int64_t heads, int64_t head_dim, int causal,
-                                             void* stream_) {
-  if (batch < 0 || seq_len < 0 || heads < 0) return B200_ERR_INVALID_ARG;
+                                             int64_t seq_len, int64_t heads, int64_t kv_heads,
+                                             int64_t head_dim, int causal, void* stream_) {
+  if (batch < 0 || seq_len < 0 || heads < 0 || kv_heads < 0) return B200_ERR_INVALID_ARG;
   if (head_dim != b200::kAttnD) return B200_ERR_INVALID_ARG;
+  if ((heads > 0 && kv_heads == 0) || (kv_heads > 0 && heads % kv_heads != 0)) return B200_ERR_INVALID_ARG;
   if (batch == 0 || seq_len == 0 || heads == 0) return B200_OK;
   if (batch > 65535 || heads > 65535 || seq_len > 0x7fffffffLL || heads * head_dim > 0x7fffffffLL)
     return B200_ERR_TOO_LARGE;
@@ -839,16 +840,18 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   int rc = current_device_state(&st);
   if (rc != B200_OK) return rc;
   const uint64_t cols = (uint64_t)(heads * head_dim);
+  const uint64_t kv_cols = (uint64_t)(kv_heads * head_dim);
   CUtensorMap tmQ, tmK, tmV, tmO;
   if ((rc = encode_3d(&tmQ, Q, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 128, true)) != B200_OK ||
-      (rc = encode_3d(&tmK, K, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 128, true)) != B200_OK ||
-      (rc = encode_3d(&tmV, V, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 64, true)) != B200_OK ||
+      (rc = encode_3d(&tmK, K, kv_cols, (uint64_t)seq_len, (uint64_t)batch, kv_cols, 64, 128, true)) != B200_OK ||
+      (rc = encode_3d(&tmV, V, kv_cols, (uint64_t)seq_len, (uint64_t)batch, kv_cols, 64, 64, true)) != B200_OK ||
       (rc = encode_3d(&tmO, O, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 32, false)) != B200_OK)
     return rc;
   b200::AttnParams p{};
   p.seq_len = (int32_t)seq_len;
   p.heads = (int32_t)heads;
   p.batch = (int32_t)batch;
+  p.group = (int32_t)(heads / kv_heads);
   p.num_q_tiles = (int32_t)((seq_len + b200::kAttnBQ - 1) / b200::kAttnBQ);
   p.causal = causal ? 1u : 0u;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);

@@ -150,13 +150,18 @@ B200_API int b200_gemm_f32(const float* A, const float* B, float* C, int64_t M, 
 /*
  * Flash attention forward, the reference's flash_attn operator
  * (flash_attn/flash_attn.cpp:5-30 and :16-25, launch_fa2_tma_lazy_rescale in
- * fa2_tma_lazy_rescale.cu): O = softmax(Q K^T / sqrt(head_dim)) V, causal or
- * not, bf16 Q, K, V, O of shape [batch, seq_len, heads, head_dim] (contiguous,
- * 16-byte aligned), head_dim = 128 (as the reference requires), fp32 softmax
- * statistics and accumulation on the tcgen05 tensor cores.
+ * fa2_tma_lazy_rescale.cu:369-451): O = softmax(Q K^T / sqrt(head_dim)) V,
+ * causal or not, bf16 Q and O of shape [batch, seq_len, heads, head_dim] and
+ * K, V of shape [batch, seq_len, kv_heads, head_dim] (all contiguous, 16-byte
+ * aligned); heads must be a multiple of kv_heads, and query head h attends
+ * with key/value head h / (heads / kv_heads) (grouped-query attention, as
+ * fa2_tma_lazy_rescale.cu:113-114).  head_dim = 128 (as the reference
+ * requires); fp32 softmax statistics and accumulation on the tcgen05 tensor
+ * cores.  No allocation; asynchronous on `stream`.
  */
 B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const void* V, void* O, int64_t batch,
-                                  int64_t seq_len, int64_t heads, int64_t head_dim, int causal, void* stream);
+                                  int64_t seq_len, int64_t heads, int64_t kv_heads, int64_t head_dim, int causal,
+                                  void* stream);
 
 /* Element type of D for b200_gemm_bf16_ex. */
 #define B200_DTYPE_BF16 0

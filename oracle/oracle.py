@@ -186,24 +186,28 @@ def epilogue(acc: np.ndarray, alpha: float = 1.0, beta: float = 0.0, c_in: np.nd
 
 
 def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool) -> np.ndarray:
-    """Exact (fp64) attention of bf16 inputs given as uint16 bit patterns, shape
-    [batch, seq, heads, head_dim]: O = softmax(Q K^T / sqrt(D), causal mask) V, the
-    operator the reference's flash_attn kernel computes and checks against
-    F.scaled_dot_product_attention (flash_attn/main.py:36-47)."""
+    """Exact (fp64) attention of bf16 inputs given as uint16 bit patterns, Q of shape
+    [batch, seq, heads, head_dim], K and V [batch, seq, kv_heads, head_dim]:
+    O = softmax(Q K^T / sqrt(D), causal mask) V, the operator the reference's
+    flash_attn kernel computes and checks against F.scaled_dot_product_attention
+    (flash_attn/main.py:36-47).  Query head h uses key/value head
+    h // (heads // kv_heads) (fa2_tma_lazy_rescale.cu:113-114)."""
     def f64(x):
         return bf16_to_f32(np.ascontiguousarray(x)).astype(np.float64)
     qf, kf, vf = f64(q), f64(k), f64(v)
     B, S, H, D = qf.shape
+    group = H // kf.shape[2]
     out = np.empty((B, S, H, D), dtype=np.float64)
     mask = np.triu(np.ones((S, S), dtype=bool), 1) if causal else None
     for b in range(B):
         for h in range(H):
-            s = qf[b, :, h, :] @ kf[b, :, h, :].T / np.sqrt(D)
+            hk = h // group
+            s = qf[b, :, h, :] @ kf[b, :, hk, :].T / np.sqrt(D)
             if mask is not None:
                 s[mask] = -np.inf
             s = s - s.max(axis=1, keepdims=True)
             p = np.exp(s)
-            out[b, :, h, :] = (p / p.sum(axis=1, keepdims=True)) @ vf[b, :, h, :]
+            out[b, :, h, :] = (p / p.sum(axis=1, keepdims=True)) @ vf[b, :, hk, :]
     return out
 
 

@@ -87,6 +87,39 @@ def test_torch_binding_rejects_bad_arguments_on_cpu():
         ext.matmul_b200_kn(a.half(), a)
 
 
+def test_attention_binding_rejects_bad_arguments_on_cpu():
+    """The reference-shaped attention binding (flash_attn/flash_attn.cpp:16-30)
+    exports both names and raises on bad input before any CUDA call."""
+    import torch
+    from b200_gemm.binding import load_attn_binding
+    ext = load_attn_binding()
+    assert hasattr(ext, "fa2_tma_lazy_rescale") and hasattr(ext, "flash_attn_b200")
+    q = torch.zeros((1, 128, 2, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ext.fa2_tma_lazy_rescale(q, q, q)
+    with pytest.raises(ValueError, match="bfloat16"):
+        ext.flash_attn_b200(q.float(), q, q, causal=False)
+    with pytest.raises(ValueError, match="4-D"):
+        ext.fa2_tma_lazy_rescale(q[0], q[0], q[0])
+
+
+def test_attention_argument_errors_without_gpu():
+    """b200_flash_attn_bf16 checks its arguments before touching the device."""
+    from b200_gemm import _lib
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    fake = P(0x10000)
+    f = lib.b200_flash_attn_bf16
+    assert f(fake, fake, fake, fake, 1, 128, 2, 2, 64, 1, None) == _lib.B200_ERR_INVALID_ARG   # head_dim 64
+    assert f(fake, fake, fake, fake, 1, 128, 6, 4, 128, 1, None) == _lib.B200_ERR_INVALID_ARG  # 6 % 4 != 0
+    assert f(fake, fake, fake, fake, 1, 128, 2, 0, 128, 1, None) == _lib.B200_ERR_INVALID_ARG  # no kv heads
+    assert f(fake, fake, fake, fake, -1, 128, 2, 2, 128, 1, None) == _lib.B200_ERR_INVALID_ARG
+    assert f(fake, fake, fake, fake, 1 << 17, 128, 2, 2, 128, 1, None) == _lib.B200_ERR_TOO_LARGE
+    assert f(fake, None, fake, fake, 1, 128, 2, 2, 128, 1, None) == _lib.B200_ERR_INVALID_ARG
+    assert f(fake, fake, P(0x10008), fake, 1, 128, 2, 2, 128, 1, None) == _lib.B200_ERR_ALIGNMENT
+    assert f(fake, fake, fake, fake, 0, 128, 2, 2, 128, 1, None) == _lib.B200_OK  # empty: nothing to do
+
+
 def test_epilogue_argument_errors_without_gpu():
     from b200_gemm import _lib
     lib = _lib.load()

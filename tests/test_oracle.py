@@ -68,6 +68,20 @@ def test_attention_known_answers():
     assert np.allclose(causal, np.cumsum(vv, axis=0) / np.arange(1, S + 1)[:, None])
 
 
+def test_attention_grouped_heads_match_repeated_heads():
+    # heads = 4, kv_heads = 2: query heads 0, 1 use key/value head 0 and 2, 3 use
+    # head 1 (fa2_tma_lazy_rescale.cu:113-114), i.e. plain attention with each
+    # key/value head repeated twice.
+    rng = np.random.default_rng(3)
+    q = o.f32_to_bf16(rng.standard_normal((2, 9, 4, 128)).astype(np.float32))
+    k = o.f32_to_bf16(rng.standard_normal((2, 9, 2, 128)).astype(np.float32))
+    v = o.f32_to_bf16(rng.standard_normal((2, 9, 2, 128)).astype(np.float32))
+    for causal in (False, True):
+        g = o.attention(q, k, v, causal)
+        r = o.attention(q, np.repeat(k, 2, axis=2), np.repeat(v, 2, axis=2), causal)
+        assert np.array_equal(g, r)
+
+
 def test_tiny_known_product():
     # 2x3 @ (2x3)^T with exactly representable values.
     a = o.f32_to_bf16(np.array([[1, 2, 3], [-1, 0.5, 4]], dtype=np.float32))
