@@ -6,21 +6,29 @@
 // h / (heads / kv_heads) (grouped-query attention, as the reference's kernel,
 // fa2_tma_lazy_rescale.cu:113-114).
 //
-// One CTA per (128 query rows, head, batch); 192 threads:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
-//               through a 2-deep ring each;
-//   warp 1      TMEM owner and single-thread tcgen05.mma issuer:
-//                 S_j = Q K_j^T   into TMEM (two buffers, S_{j+1} is computed
-//                                 while the softmax works on S_j),
-//                 O  += P_j V_j   into TMEM (A = P from shared memory,
-//                                 B = V tile in its natural [key][d] layout,
-//                                 i.e. an MN-major operand);
-//   warps 2..5  softmax, one thread per query row (= TMEM lane): S row from
-//               TMEM, running max and sum in fp32 (exp2 domain), P row as
-//               bf16 into 128B-swizzled shared memory; lazy rescaling — the
-//               running max, and with it O in TMEM, is only moved when the row
-//               max grows by more than 2^8 — and at the end O / l -> bf16 ->
-//               TMA store.
+// One CTA per (two 128-row query tiles, head, batch); 320 threads:
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128
+//               keys through a 2-deep ring each (each K and V tile serves both
+//               query tiles);
+//   warp 1      TMEM owner and single-thread tcgen05.mma issuer, for query
+//               tile i = 0, 1:
+//                 S_i  = Q_i K_j^T  into TMEM columns [128 i, 128 i + 128),
+//                 O_i += P_i V_j    into TMEM columns [256 + 128 i, ...), A = P_i
+//                                   read from TMEM, where the softmax wrote it
+//                                   (bf16) over S_i, B = the V tile in its
+//                                   natural [key][d] layout (an MN-major operand);
+//               issued in the order P_0 V_j, S_0 (j+1), P_1 V_j, S_1 (j+1), so
+//               that each softmax warpgroup works while the tensor cores run
+//               the other tile's two products;
+//   warps 2..5  softmax of query tile 0, warps 6..9 of tile 1: one thread per
+//               query row (= TMEM lane).  S row from TMEM, running max and sum
+//               in fp32 (exp2 domain), P row as bf16 back into TMEM; lazy
+//               rescaling — the running max, and with it O in TMEM, is only
+//               moved when the row max grows by more than 2^8 — and at the end
+//               O / l -> bf16 -> TMA store (staged in the tile's Q buffer).
+// The exponentials are the softmax's bottleneck (16 per clock per SM on the
+// MUFU unit, the same time as the tile's MMAs): a quarter of them are computed
+// on the FMA pipe instead (poly_exp2x2).
 // Every wait is bounded (status bits on expiry), as in the GEMM kernels.
 #pragma once
 
@@ -34,9 +42,12 @@
 namespace b200 {
 
 constexpr int kAttnD = 128;      // head dimension
-constexpr int kAttnBQ = 128;     // query rows per CTA (UMMA M, TMEM lanes)
+constexpr int kAttnBQ = 128;     // query rows per tile (UMMA M, TMEM lanes)
 constexpr int kAttnBKV = 128;    // keys per tile
+constexpr int kAttnQTiles = 2;   // query tiles per CTA, one softmax warpgroup each
 constexpr int kAttnStages = 2;   // K and V ring depth
+constexpr int kAttnThreads = 64 + kAttnQTiles * 128;
+constexpr int kAttnPolyEvery = 4;  // every 4th pair of exponentials on the FMA pipe (0: none)
 constexpr float kAttnRescaleLog2 = 8.0f;  // lazy rescale threshold (P stays <= 2^8)
 
 struct AttnParams {
@@ -51,13 +62,12 @@ struct AttnParams {
 
 struct AttnSmemPlan {
   static constexpr int kTileBytes = 128 * 128 * 2;  // any 128 x 128 bf16 tile: 32 KiB
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kTileBytes;
+  static constexpr int kOffQ = 0;                   // kAttnQTiles tiles; O staging at the end
+  static constexpr int kOffK = kOffQ + kAttnQTiles * kTileBytes;
   static constexpr int kOffV = kOffK + kAttnStages * kTileBytes;
-  static constexpr int kOffP = kOffV + kAttnStages * kTileBytes;  // P, then the O staging at the end
-  static constexpr int kOffBar = kOffP + kTileBytes;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_empty[2], p_full, o_done, drain
-  static constexpr int kNumBars = 1 + 4 * kAttnStages + 4 + 3;
+  static constexpr int kOffBar = kOffV + kAttnStages * kTileBytes;
+  // q_full[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain
+  static constexpr int kNumBars = 3 * kAttnQTiles + 4 * kAttnStages + kAttnQTiles + 1;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAbort = kOffTmemHolder + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -71,14 +81,76 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair, on the FMA pipe instead of the MUFU unit, for x <= 2^7
+// (clamped below at -125 so the result stays a normal float; those values
+// are below 2^-124 and vanish against the row sum, which is >= 1).
+// x = n + f with n = rint(x) (adding 1.5 * 2^23 leaves rint(x) in the low
+// mantissa bits) and |f| <= 1/2; 2^f from a cubic fitted for this build by
+// Lawson's iteration to minimax relative error on [-1/2, 1/2] (7.5e-5,
+// against the 2^-9 rounding of P to bf16); n is added into the exponent.
+__device__ __forceinline__ float2 poly_exp2x2(float2 x) {
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 shift = make_float2(12582912.0f, 12582912.0f);
+  const float2 t = __fadd2_rn(x, shift);
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 y = __ffma2_rn(make_float2(0x1.c3f76p-5f, 0x1.c3f76p-5f), f, make_float2(0x1.f0de1cp-3f, 0x1.f0de1cp-3f));
+  y = __ffma2_rn(y, f, make_float2(0x1.62f31ap-1f, 0x1.62f31ap-1f));
+  y = __ffma2_rn(y, f, make_float2(0x1.fff692p-1f, 0x1.fff692p-1f));
+  return make_float2(__uint_as_float(__float_as_uint(y.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(y.y) + (__float_as_uint(t.y) << 23)));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// P = 2^(x * scale - m_use) for one row of 128 scores, packed as bf16 pairs
+// (key 2c in the low half of word c), and its sum.  kPoly: every
+// kAttnPolyEvery-th pair goes through poly_exp2x2 (only for tiles without
+// masked keys: there x = -inf must give exactly 0).
+template <bool kPoly>
+__device__ __forceinline__ float row_exp(const float (&x)[kAttnBKV], float scale, float m_use,
+                                         uint32_t (&pw)[2][32]) {
+  const float2 sc = make_float2(scale, scale);
+  const float2 nm = make_float2(-m_use, -m_use);
+  float2 acc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int c = 0; c < kAttnBKV; c += 2) {
+    const float2 t = __ffma2_rn(make_float2(x[c], x[c + 1]), sc, nm);
+    float2 e;
+    if (kPoly && kAttnPolyEvery > 0 && ((c >> 1) % (kAttnPolyEvery > 0 ? kAttnPolyEvery : 1)) == kAttnPolyEvery - 1) {
+      e = poly_exp2x2(t);
+    } else {
+      e = make_float2(fast_exp2(t.x), fast_exp2(t.y));
+    }
+    acc[(c >> 1) & 3] = __fadd2_rn(acc[(c >> 1) & 3], e);
+    pw[c >> 6][(c >> 1) & 31] = pack_bf16x2(e.x, e.y);
+  }
+  const float2 s01 = __fadd2_rn(acc[0], acc[1]);
+  const float2 s23 = __fadd2_rn(acc[2], acc[3]);
+  const float2 s = __fadd2_rn(s01, s23);
+  return s.x + s.y;
+}
+
 __device__ __forceinline__ void attn_raise(const AttnParams& p, volatile uint32_t* abort_flag, uint32_t code) {
   *abort_flag = 1u;
   if (p.status != nullptr) atomicOr(p.status, code);
 }
 
-// Grid (num_q_tiles, heads, batch).  Query tiles are taken in reverse order so
-// that, with a causal mask, the longest rows start first.
-__global__ void __launch_bounds__(kNumThreads, 1)
+// Grid (ceil(num_q_tiles / 2), heads, batch).  Query tile pairs are taken in
+// reverse order so that, with a causal mask, the longest rows start first.
+__global__ void __launch_bounds__(kAttnThreads, 1)
     flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                           const __grid_constant__ AttnParams p) {
@@ -93,45 +165,50 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t sQ = base + Plan::kOffQ;
   const uint32_t sK = base + Plan::kOffK;
   const uint32_t sV = base + Plan::kOffV;
-  const uint32_t sP = base + Plan::kOffP;
   const uint32_t bar0 = base + Plan::kOffBar;
-  const uint32_t q_full = bar0;
-  auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return bar0 + 8u * (1 + kAttnStages + s); };
-  auto v_full = [&](int s) { return bar0 + 8u * (1 + 2 * kAttnStages + s); };
-  auto v_empty = [&](int s) { return bar0 + 8u * (1 + 3 * kAttnStages + s); };
-  auto s_full = [&](int b) { return bar0 + 8u * (1 + 4 * kAttnStages + b); };
-  auto s_empty = [&](int b) { return bar0 + 8u * (3 + 4 * kAttnStages + b); };
-  const uint32_t p_full = bar0 + 8u * (5 + 4 * kAttnStages);
-  const uint32_t o_done = p_full + 8u;
-  const uint32_t drain = o_done + 8u;  // every MMA issued has completed (teardown)
+  auto q_full = [&](int i) { return bar0 + 8u * i; };
+  auto k_full = [&](int s) { return bar0 + 8u * (kAttnQTiles + s); };
+  auto k_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + kAttnStages + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (kAttnQTiles + 2 * kAttnStages + s); };
+  auto v_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + 3 * kAttnStages + s); };
+  auto s_full = [&](int i) { return bar0 + 8u * (kAttnQTiles + 4 * kAttnStages + i); };
+  auto p_full = [&](int i) { return bar0 + 8u * (2 * kAttnQTiles + 4 * kAttnStages + i); };
+  auto o_full = [&](int i) { return bar0 + 8u * (3 * kAttnQTiles + 4 * kAttnStages + i); };
+  const uint32_t drain = bar0 + 8u * (4 * kAttnQTiles + 4 * kAttnStages);  // every MMA issued has completed
   volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
-  const int qt = p.num_q_tiles - 1 - (int)blockIdx.x;
+  const int qt0 = kAttnQTiles * ((int)gridDim.x - 1 - (int)blockIdx.x);  // first query tile of the CTA
   const int head = blockIdx.y;
   const int bat = blockIdx.z;
   const int kv_tiles_all = (p.seq_len + kAttnBKV - 1) / kAttnBKV;
-  const int n_kv = p.causal ? min(qt + 1, kv_tiles_all) : kv_tiles_all;
-  const int col0 = head * kAttnD;  // column of this head in the [seq, heads * D] view
-  const int kv_col0 = (head / p.group) * kAttnD;  // its key/value head in [seq, kv_heads * D]
+  // Key tiles query tile qt reads (the causal mask ends at the diagonal tile);
+  // 0 for a second tile past the end of the sequence.
+  auto kv_tiles = [&](int qt) {
+    return qt >= p.num_q_tiles ? 0 : (p.causal ? min(qt + 1, kv_tiles_all) : kv_tiles_all);
+  };
+  const int n0 = kv_tiles(qt0);
+  const int n1 = kv_tiles(qt0 + 1);  // >= n0, or 0
+  const int n_max = max(n0, n1);
+  const int n_q = n1 > 0 ? 2 : 1;    // query tiles this CTA holds
+  const int col0 = head * kAttnD;                  // column of this head in the [seq, heads * D] view
+  const int kv_col0 = (head / p.group) * kAttnD;   // its key/value head in [seq, kv_heads * D]
 
   if (warp == 0 && lane == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < kAttnQTiles; ++i) {
+      mbar_init(q_full(i), 1);
+      mbar_init(s_full(i), 1);
+      mbar_init(p_full(i), 4);
+      mbar_init(o_full(i), 1);
+    }
     for (int s = 0; s < kAttnStages; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), kEpiWarps);
-    }
-    mbar_init(p_full, kEpiWarps);
-    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0u;
     fence_mbar_init();
@@ -147,7 +224,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_holder;  // S buffers at columns 0 and 128, O at 256
+  const uint32_t tmem_base = *tmem_holder;  // S_i at columns 128 i, O_i at 256 + 128 i
   pdl_launch_dependents();
   pdl_wait();
 
@@ -156,11 +233,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (lane == 0) {
       const uint64_t pol_keep = l2_policy_evict_last();  // K, V: read by every query tile of the head
       const uint64_t pol_once = l2_policy_evict_first();  // Q: read once
-      mbar_arrive_expect_tx(q_full, Plan::kTileBytes);
-      for (int i = 0; i < 2; ++i) tma_load_3d(sQ + i * 16384, &tmQ, q_full, col0 + 64 * i, qt * kAttnBQ, bat, pol_once);
+      for (int i = 0; i < n_q; ++i) {
+        mbar_arrive_expect_tx(q_full(i), Plan::kTileBytes);
+        for (int h = 0; h < 2; ++h) {
+          tma_load_3d(sQ + i * Plan::kTileBytes + h * 16384, &tmQ, q_full(i), col0 + 64 * h,
+                      (qt0 + i) * kAttnBQ, bat, pol_once);
+        }
+      }
       bool ok = true;
       int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int j = 0; j < n_max && ok; ++j) {
         const int s = j & 1;
         const uint32_t ph = (uint32_t)(j >> 1) & 1u;
         if (!mbar_wait(k_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
@@ -168,8 +250,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(k_full(s), Plan::kTileBytes);
-        for (int i = 0; i < 2; ++i) {
-          tma_load_3d(sK + s * Plan::kTileBytes + i * 16384, &tmK, k_full(s), kv_col0 + 64 * i, j * kAttnBKV, bat,
+        for (int h = 0; h < 2; ++h) {
+          tma_load_3d(sK + s * Plan::kTileBytes + h * 16384, &tmK, k_full(s), kv_col0 + 64 * h, j * kAttnBKV, bat,
                       pol_keep);
         }
         ++k_issued;
@@ -180,8 +262,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         mbar_arrive_expect_tx(v_full(s), Plan::kTileBytes);
         // V tile as two 64-key halves, each two 64-column atoms of [64 keys][64 d].
         for (int hk = 0; hk < 2; ++hk) {
-          for (int i = 0; i < 2; ++i) {
-            tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + i * 8192, &tmV, v_full(s), kv_col0 + 64 * i,
+          for (int h = 0; h < 2; ++h) {
+            tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + h * 8192, &tmV, v_full(s), kv_col0 + 64 * h,
                         j * kAttnBKV + 64 * hk, bat, pol_keep);
           }
         }
@@ -189,8 +271,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       if (!ok) attn_raise(p, abort_flag, kDevTimeoutProducer);
       // Let the copies in flight land before the CTA can leave.
-      if (!mbar_wait(q_full, 0u, p.timeout_ns, nullptr)) attn_raise(p, abort_flag, kDevTimeoutDrain);
       bool drained = true;
+      for (int i = 0; drained && i < n_q; ++i) drained = mbar_wait(q_full(i), 0u, p.timeout_ns, nullptr);
       for (int j = k_issued - 1; drained && j >= 0 && j >= k_issued - kAttnStages; --j) {
         drained = mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
       }
@@ -204,70 +286,103 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ---- MMA issuer ----------------------------------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(kAttnBQ, kAttnBKV, false, false);  // Q (K-major) x K^T (K-major)
-      constexpr uint32_t idesc_o = idesc_bf16_f32(kAttnBQ, kAttnD, false, true);     // P (K-major) x V (MN-major)
+      constexpr uint32_t idesc_o = idesc_bf16_f32(kAttnBQ, kAttnD, false, true);     // P (TMEM) x V (MN-major)
       // 16-wide K slices: K-major operands step 32 B inside a 64-wide atom
       // and 16 KiB between the two atoms; the MN-major V steps 16 keys =
-      // 2 KiB inside a 64-key half and 16 KiB between halves.
+      // 2 KiB inside a 64-key half and 16 KiB between halves; P in TMEM
+      // steps 8 columns (16 bf16).
       auto kmajor = [](uint32_t tile, int k) {
         return smem_desc_sw128(tile + (uint32_t)((k >> 2) * 16384 + (k & 3) * 32), 16, 1024);
       };
       auto vdesc = [](uint32_t tile, int k) {
         return smem_desc_sw128(tile + (uint32_t)((k >> 2) * 16384 + (k & 3) * 2048), 8192, 1024);
       };
-      bool ok = mbar_wait(q_full, 0u, p.timeout_ns, abort_flag);
-      auto pv = [&](int i) {
-        if (!ok) return;
-        if (!mbar_wait(p_full, (uint32_t)i & 1u, p.timeout_ns, abort_flag) ||
-            !mbar_wait(v_full(i & 1), (uint32_t)(i >> 1) & 1u, p.timeout_ns, abort_flag)) {
-          ok = false;
-          return;
+      auto issue_s = [&](int i, int j) {
+        const uint32_t qa = sQ + (uint32_t)(i * Plan::kTileBytes);
+        const uint32_t kt = sK + (uint32_t)((j & 1) * Plan::kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kAttnD / kUmmaK; ++k) {
+          umma_bf16(tmem_base + (uint32_t)(i * 128), kmajor(qa, k), kmajor(kt, k), idesc_s, k > 0 ? 1u : 0u);
         }
-        tc_fence_after();
-        const uint32_t vt = sV + (uint32_t)((i & 1) * Plan::kTileBytes);
+      };
+      auto issue_pv = [&](int i, int j) {
+        const uint32_t vt = sV + (uint32_t)((j & 1) * Plan::kTileBytes);
 #pragma unroll
         for (int k = 0; k < kAttnBKV / kUmmaK; ++k) {
-          umma_bf16(tmem_base + 256u, kmajor(sP, k), vdesc(vt, k), idesc_o, (i > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem_base + 256u + (uint32_t)(i * 128), tmem_base + (uint32_t)(i * 128 + k * 8),
+                       vdesc(vt, k), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(v_empty(i & 1));
-        umma_commit(o_done);
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
+      auto wait_k = [&](int j) { return mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag); };
+      bool ok = true;
+      for (int i = 0; ok && i < n_q; ++i) ok = mbar_wait(q_full(i), 0u, p.timeout_ns, abort_flag);
+      if (ok && n_max > 0) {
+        ok = wait_k(0);
+        if (ok) {
+          tc_fence_after();
+          for (int i = 0; i < n_q; ++i) {
+            issue_s(i, 0);
+            umma_commit(s_full(i));
+          }
+          umma_commit(k_empty(0));
+        }
+      }
+      const int n_tiles[2] = {n0, n1};
+      for (int j = 0; j < n_max && ok; ++j) {
         const int s = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(k_full(s), ph, p.timeout_ns, abort_flag) ||
-            !mbar_wait(s_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
+        if (!mbar_wait(v_full(s), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t kt = sK + (uint32_t)(s * Plan::kTileBytes);
+        bool k_ready = false;
 #pragma unroll
-        for (int k = 0; k < kAttnD / kUmmaK; ++k) {
-          umma_bf16(tmem_base + (uint32_t)(s * kAttnBKV), kmajor(sQ, k), kmajor(kt, k), idesc_s, k > 0 ? 1u : 0u);
+        for (int i = 0; i < kAttnQTiles; ++i) {
+          if (!ok || j >= n_tiles[i]) continue;
+          if (!mbar_wait(p_full(i), (uint32_t)j & 1u, p.timeout_ns, abort_flag)) {
+            ok = false;
+            continue;
+          }
+          tc_fence_after();
+          issue_pv(i, j);
+          if (i == kAttnQTiles - 1 || j >= n_tiles[kAttnQTiles - 1]) umma_commit(v_empty(s));  // last user of V_j
+          if (j + 1 < n_tiles[i]) {
+            if (!k_ready) {
+              if (!wait_k(j + 1)) {
+                ok = false;
+                continue;
+              }
+              k_ready = true;
+              tc_fence_after();
+            }
+            issue_s(i, j + 1);
+            umma_commit(s_full(i));
+          } else {
+            umma_commit(o_full(i));
+          }
         }
-        umma_commit(k_empty(s));
-        umma_commit(s_full(s));
-        if (j >= 1) pv(j - 1);
+        if (ok && j + 1 < n_max) umma_commit(k_empty((j + 1) & 1));
       }
-      if (ok && n_kv > 0) pv(n_kv - 1);
       if (!ok) attn_raise(p, abort_flag, kDevTimeoutMma);
       umma_commit(drain);
       if (!mbar_wait(drain, 0u, p.timeout_ns, nullptr)) attn_raise(p, abort_flag, kDevTimeoutDrain);
     }
     __syncwarp();
   } else {
-    // ---- softmax + epilogue (warps 2..5) -------------------------------------
+    // ---- softmax + epilogue (warps 2..5: tile 0, warps 6..9: tile 1) ----------
+    const int tile = (warp - 2) >> 2;
     const int qw = warp & 3;                // TMEM lane quarter this warp may access
     const int row = qw * 32 + (int)lane;     // query row in the tile
+    const int qt = qt0 + tile;
+    const int n_kv = tile == 0 ? n0 : n1;
     const int q_idx = qt * kAttnBQ + row;    // query position
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + (uint32_t)(tile * 128);
+    const uint32_t tO = tmem_base + lane_off + 256u + (uint32_t)(tile * 128);
     float m = -INFINITY;  // running max (exp2 domain) the stored P and O refer to
     float l = 0.0f;       // running sum of P
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int s = j & 1;
-      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-      const bool got = mbar_wait(s_full(s), ph, p.timeout_ns, abort_flag);
+      const bool got = mbar_wait(s_full(tile), (uint32_t)j & 1u, p.timeout_ns, abort_flag);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
@@ -275,89 +390,57 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       tc_fence_after();
       float x[kAttnBKV];
       {
-        uint32_t r[32];
+        uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < kAttnBKV / 32; ++c) {
-          tmem_ld_32x32b_x32(tmem_base + lane_off + (uint32_t)(s * kAttnBKV + c * 32), r);
-          tmem_ld_wait_regs(r);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tS + (uint32_t)(c * 32), r[c]);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]);
+        for (int c = 0; c < 4; ++c) tmem_ld_wait_regs(r[c]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[c][i]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(s));  // S buffer s may be overwritten by S_{j+2}
       const int kv0 = j * kAttnBKV;
       const bool diag = p.causal && kv0 + kAttnBKV > qt * kAttnBQ;  // the tile crossing the diagonal
-      // Scale into the exp2 domain and take the row max.  Eight independent
-      // partial maxima (and sums below): one thread owns the whole row, so a
-      // single dependency chain over 128 keys would serialise on latency.
       // Only the diagonal tile and a tile past the sequence end need masks:
       // keys c >= lim are masked.
       const bool masked = diag || kv0 + kAttnBKV > p.seq_len;
-      const int lim = min(p.seq_len - kv0, diag ? q_idx - kv0 + 1 : kAttnBKV);
+      if (masked) {
+        const int lim = min(p.seq_len - kv0, diag ? q_idx - kv0 + 1 : kAttnBKV);
+#pragma unroll
+        for (int c = 0; c < kAttnBKV; ++c) x[c] = c < lim ? x[c] : -INFINITY;
+      }
+      // Row max of the raw scores (the scale is positive): eight independent
+      // chains of three-input maxima, so one thread's row is not one long
+      // dependency chain.
       float mxs[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
-      if (!masked) {
 #pragma unroll
-        for (int c = 0; c < kAttnBKV; ++c) {
-          x[c] *= p.scale_log2;
-          mxs[c & 7] = fmaxf(mxs[c & 7], x[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kAttnBKV; ++c) {
-          x[c] = c < lim ? x[c] * p.scale_log2 : -INFINITY;
-          mxs[c & 7] = fmaxf(mxs[c & 7], x[c]);
-        }
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
-      const float m_new = fmaxf(m, mx);
+      for (int c = 0; c < kAttnBKV; c += 2) mxs[(c >> 1) & 7] = max3f(mxs[(c >> 1) & 7], x[c], x[c + 1]);
+      const float mx = max3f(max3f(mxs[0], mxs[1], mxs[2]), max3f(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
+      const float m_new = fmaxf(m, mx * p.scale_log2);
       // Move the reference max only when the row max grew by more than 2^8
       // (or nothing was seen yet): P stays below 2^8, and O is rescaled rarely.
       const bool move = (m == -INFINITY) ? (m_new != -INFINITY) : (m_new > m + kAttnRescaleLog2);
       const float factor = (move && m != -INFINITY) ? fast_exp2(m - m_new) : 1.0f;
-      // P and its row sum with the max the row will use from now on — all
-      // before waiting for the previous P V product, so the exponentials
-      // overlap that MMA; P is kept packed as bf16 pairs.
       const float m_next = move ? m_new : m;
       const float m_use = (m_next == -INFINITY) ? 0.0f : m_next;
-      float sums[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
-      uint32_t pw[kAttnBKV / 2];
-#pragma unroll
-      for (int c = 0; c < kAttnBKV; c += 2) {
-        // exp2(-inf) is +0: masked keys need no test.
-        const float e0 = fast_exp2(x[c] - m_use);
-        const float e1 = fast_exp2(x[c + 1] - m_use);
-        sums[(c >> 1) & 7] += e0 + e1;
-        __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
-        pw[c / 2] = *reinterpret_cast<uint32_t*>(&h);
-      }
-      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-      if (j > 0) {
-        // P_{j-1} V_{j-1} done: the P buffer is free and O is stable.
-        const bool prev = mbar_wait(o_done, (uint32_t)(j - 1) & 1u, p.timeout_ns, abort_flag);
-        if (!__all_sync(0xffffffffu, prev)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, move && factor != 1.0f)) {
-          uint32_t r[32];
+      uint32_t pw[2][32];
+      const float sum = masked ? row_exp<false>(x, p.scale_log2, m_use, pw) : row_exp<true>(x, p.scale_log2, m_use, pw);
+      if (j > 0 && __any_sync(0xffffffffu, move && factor != 1.0f)) {
+        // S_i(j) was issued after P_i(j-1) V(j-1), and its completion signal
+        // covers that product: O is stable until this warpgroup's P is in.
+        uint32_t r[32];
 #pragma unroll 1
-          for (int c = 0; c < kAttnD / 32; ++c) {
-            const uint32_t ta = tmem_base + lane_off + 256u + (uint32_t)(c * 32);
-            tmem_ld_32x32b_x32(ta, r);
-            tmem_ld_wait_regs(r);
+        for (int c = 0; c < kAttnD / 32; ++c) {
+          const uint32_t ta = tO + (uint32_t)(c * 32);
+          tmem_ld_32x32b_x32(ta, r);
+          tmem_ld_wait_regs(r);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tmem_st_32x32b_x32(ta, r);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tmem_st_32x32b_x32(ta, r);
         }
       }
       if (move) {
@@ -365,40 +448,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         m = m_new;
       }
       l += sum;
-      // P row -> shared memory, bf16, 128B-swizzled K-major (keys contiguous):
-      // two atoms of 64 keys, 16-byte chunk c of row r at chunk c ^ (r & 7).
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        const uint32_t row_addr = sP + (uint32_t)(a * 16384 + row * 128);
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const int w0 = a * 32 + cc * 4;
-          const uint32_t dst = row_addr + (((uint32_t)cc ^ ((uint32_t)row & 7u)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(pw[w0]), "r"(pw[w0 + 1]),
-                       "r"(pw[w0 + 2]), "r"(pw[w0 + 3])
-                       : "memory");
-        }
-      }
-      fence_proxy_async_smem();
+      // P row -> TMEM over the first 64 columns of S (two bf16 per column).
+      tmem_st_32x32b_x32(tS, pw[0]);
+      tmem_st_32x32b_x32(tS + 32u, pw[1]);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full(tile));
     }
     if (!ok) {
       if (lane == 0) attn_raise(p, abort_flag, kDevTimeoutEpilogue);
     } else if (n_kv > 0) {
-      // O / l -> bf16 -> TMA store, through this warp's 8 KiB of the (now
-      // idle) P buffer: two [32 rows][64 d] swizzled chunks.
-      const bool last = mbar_wait(o_done, (uint32_t)(n_kv - 1) & 1u, p.timeout_ns, abort_flag);
+      // O / l -> bf16 -> TMA store, through this warp's 8 KiB of the tile's
+      // Q buffer (idle once the last product is done): two [32 rows][64 d]
+      // swizzled chunks.
+      const bool last = mbar_wait(o_full(tile), 0u, p.timeout_ns, abort_flag);
       if (__all_sync(0xffffffffu, last)) {
         tc_fence_after();
         const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
-        const uint32_t stage = sP + (uint32_t)(qw * 8192);
+        const uint32_t stage = sQ + (uint32_t)(tile * Plan::kTileBytes + qw * 8192);
 #pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           uint32_t lo[32], hi[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_off + 256u + (uint32_t)(half * 64), lo);
-          tmem_ld_32x32b_x32(tmem_base + lane_off + 256u + (uint32_t)(half * 64 + 32), hi);
+          tmem_ld_32x32b_x32(tO + (uint32_t)(half * 64), lo);
+          tmem_ld_32x32b_x32(tO + (uint32_t)(half * 64 + 32), hi);
           tmem_ld_wait_regs(lo);
           tmem_ld_wait_regs(hi);
 #pragma unroll

@@ -861,8 +861,9 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3((unsigned)p.num_q_tiles, (unsigned)heads, (unsigned)batch);
-  cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
+  cfg.gridDim = dim3((unsigned)((p.num_q_tiles + b200::kAttnQTiles - 1) / b200::kAttnQTiles), (unsigned)heads,
+                     (unsigned)batch);
+  cfg.blockDim = dim3(b200::kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = b200::AttnSmemPlan::kAllocBytes;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream_);
   cfg.attrs = attr;
