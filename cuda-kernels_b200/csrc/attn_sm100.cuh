@@ -6,11 +6,13 @@
 // h / (heads / kv_heads) (grouped-query attention, as the reference's kernel,
 // fa2_tma_lazy_rescale.cu:113-114).
 //
-// One CTA per (two 128-row query tiles, head, batch); 320 threads:
-//   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128
+// One CTA per (two 128-row query tiles, head, batch); 384 threads in three
+// warpgroups:
+//   warps 0..3  softmax of query tile 0, warps 4..7 of tile 1 (below);
+//   warp 8      TMA producer: both Q tiles once, then K and V tiles of 128
 //               keys through a 2-deep ring each (each K and V tile serves both
 //               query tiles);
-//   warp 1      TMEM owner and single-thread tcgen05.mma issuer, for query
+//   warp 9      TMEM owner and single-thread tcgen05.mma issuer, for query
 //               tile i = 0, 1:
 //                 S_i  = Q_i K_j^T  into TMEM columns [128 i, 128 i + 128),
 //                 O_i += P_i V_j    into TMEM columns [256 + 128 i, ...), A = P_i
@@ -20,15 +22,17 @@
 //               issued in the order P_0 V_j, S_0 (j+1), P_1 V_j, S_1 (j+1), so
 //               that each softmax warpgroup works while the tensor cores run
 //               the other tile's two products;
-//   warps 2..5  softmax of query tile 0, warps 6..9 of tile 1: one thread per
-//               query row (= TMEM lane).  S row from TMEM, running max and sum
-//               in fp32 (exp2 domain), P row as bf16 back into TMEM; lazy
-//               rescaling — the running max, and with it O in TMEM, is only
-//               moved when the row max grows by more than 2^8 — and at the end
-//               O / l -> bf16 -> TMA store (staged in the tile's Q buffer).
-// The exponentials are the softmax's bottleneck (16 per clock per SM on the
-// MUFU unit, the same time as the tile's MMAs): a quarter of them are computed
-// on the FMA pipe instead (poly_exp2x2).
+//   warps 10,11 idle.
+// Softmax: one thread per query row (= TMEM lane) holds the row's 128 scores
+// in registers (the third warpgroup gives up registers with setmaxnreg so
+// that the softmax warpgroups have 224 each): S row from TMEM, running max and
+// sum in fp32 (exp2 domain), P row as bf16 back into TMEM; lazy rescaling —
+// the running max, and with it O in TMEM, is only moved when the row max grows
+// by more than 2^8 — and at the end O / l -> bf16 -> TMA store (staged in the
+// tile's Q buffer).
+// The exponentials run on the MUFU unit (16 per clock per SM, as long as the
+// tile's MMAs); poly_exp2x2 can move a share of them to the FMA pipe
+// (kAttnPolyEvery).
 // Every wait is bounded (status bits on expiry), as in the GEMM kernels.
 #pragma once
 
@@ -46,8 +50,19 @@ constexpr int kAttnBQ = 128;     // query rows per tile (UMMA M, TMEM lanes)
 constexpr int kAttnBKV = 128;    // keys per tile
 constexpr int kAttnQTiles = 2;   // query tiles per CTA, one softmax warpgroup each
 constexpr int kAttnStages = 2;   // K and V ring depth
-constexpr int kAttnThreads = 64 + kAttnQTiles * 128;
-constexpr int kAttnPolyEvery = 4;  // every 4th pair of exponentials on the FMA pipe (0: none)
+constexpr int kAttnThreads = 128 * (kAttnQTiles + 1);
+constexpr int kAttnProducerWarp = 4 * kAttnQTiles;
+constexpr int kAttnMmaWarp = kAttnProducerWarp + 1;
+// Registers per thread: at launch (the kernel is compiled to exactly this),
+// after reallocation for the producer/MMA warpgroup and for the softmax
+// warpgroups.  128 * 56 + 256 * 224 = 384 * 168.
+constexpr uint32_t kAttnRegsLaunch = 168, kAttnRegsOther = 56, kAttnRegsSoftmax = 224;
+static_assert(128 * kAttnRegsOther + kAttnQTiles * 128 * kAttnRegsSoftmax <= kAttnThreads * kAttnRegsLaunch,
+              "register reallocation exceeds the launch pool");
+// Every kAttnPolyEvery-th pair of exponentials on the FMA pipe (0: none).
+// Measured on B200: every 4th pair cost 2 %, every 2nd 7 % (the softmax is
+// bound by latency and issue, not by the MUFU rate), so it is off.
+constexpr int kAttnPolyEvery = 0;
 constexpr float kAttnRescaleLog2 = 8.0f;  // lazy rescale threshold (P stays <= 2^8)
 
 struct AttnParams {
@@ -148,8 +163,9 @@ __device__ __forceinline__ void attn_raise(const AttnParams& p, volatile uint32_
   if (p.status != nullptr) atomicOr(p.status, code);
 }
 
-// Grid (ceil(num_q_tiles / 2), heads, batch).  Query tile pairs are taken in
-// reverse order so that, with a causal mask, the longest rows start first.
+// Grid (heads * batch, ceil(num_q_tiles / 2)).  Blocks start in linear
+// order, x fastest, and query tile pairs are taken in reverse order of y: the
+// longest causal rows of every head start first (longest-first scheduling).
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -180,9 +196,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
-  const int qt0 = kAttnQTiles * ((int)gridDim.x - 1 - (int)blockIdx.x);  // first query tile of the CTA
-  const int head = blockIdx.y;
-  const int bat = blockIdx.z;
+  const int qt0 = kAttnQTiles * ((int)gridDim.y - 1 - (int)blockIdx.y);  // first query tile of the CTA
+  const int head = (int)blockIdx.x % p.heads;
+  const int bat = (int)blockIdx.x / p.heads;
   const int kv_tiles_all = (p.seq_len + kAttnBKV - 1) / kAttnBKV;
   // Key tiles query tile qt reads (the causal mask ends at the diagonal tile);
   // 0 for a second tile past the end of the sequence.
@@ -196,7 +212,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int col0 = head * kAttnD;                  // column of this head in the [seq, heads * D] view
   const int kv_col0 = (head / p.group) * kAttnD;   // its key/value head in [seq, kv_heads * D]
 
-  if (warp == 0 && lane == 0) {
+  if (warp == kAttnProducerWarp && lane == 0) {
     for (int i = 0; i < kAttnQTiles; ++i) {
       mbar_init(q_full(i), 1);
       mbar_init(s_full(i), 1);
@@ -217,7 +233,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmO);
   }
-  if (warp == 1) {
+  if (warp == kAttnMmaWarp) {
     tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_holder)), 512);
     tmem_relinquish();
   }
@@ -228,148 +244,152 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   pdl_launch_dependents();
   pdl_wait();
 
-  if (warp == 0) {
-    // ---- TMA producer ------------------------------------------------------
-    if (lane == 0) {
-      const uint64_t pol_keep = l2_policy_evict_last();  // K, V: read by every query tile of the head
-      const uint64_t pol_once = l2_policy_evict_first();  // Q: read once
-      for (int i = 0; i < n_q; ++i) {
-        mbar_arrive_expect_tx(q_full(i), Plan::kTileBytes);
-        for (int h = 0; h < 2; ++h) {
-          tma_load_3d(sQ + i * Plan::kTileBytes + h * 16384, &tmQ, q_full(i), col0 + 64 * h,
-                      (qt0 + i) * kAttnBQ, bat, pol_once);
-        }
-      }
-      bool ok = true;
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n_max && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(k_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(k_full(s), Plan::kTileBytes);
-        for (int h = 0; h < 2; ++h) {
-          tma_load_3d(sK + s * Plan::kTileBytes + h * 16384, &tmK, k_full(s), kv_col0 + 64 * h, j * kAttnBKV, bat,
-                      pol_keep);
-        }
-        ++k_issued;
-        if (!mbar_wait(v_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(v_full(s), Plan::kTileBytes);
-        // V tile as two 64-key halves, each two 64-column atoms of [64 keys][64 d].
-        for (int hk = 0; hk < 2; ++hk) {
+  if (warp >= kAttnProducerWarp) {
+    setmaxnreg_dec<kAttnRegsOther>();
+    if (warp == kAttnProducerWarp) {
+      // ---- TMA producer ------------------------------------------------------
+      if (lane == 0) {
+        const uint64_t pol_keep = l2_policy_evict_last();  // K, V: read by every query tile of the head
+        const uint64_t pol_once = l2_policy_evict_first();  // Q: read once
+        for (int i = 0; i < n_q; ++i) {
+          mbar_arrive_expect_tx(q_full(i), Plan::kTileBytes);
           for (int h = 0; h < 2; ++h) {
-            tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + h * 8192, &tmV, v_full(s), kv_col0 + 64 * h,
-                        j * kAttnBKV + 64 * hk, bat, pol_keep);
+            tma_load_3d(sQ + i * Plan::kTileBytes + h * 16384, &tmQ, q_full(i), col0 + 64 * h,
+                        (qt0 + i) * kAttnBQ, bat, pol_once);
           }
         }
-        ++v_issued;
-      }
-      if (!ok) attn_raise(p, abort_flag, kDevTimeoutProducer);
-      // Let the copies in flight land before the CTA can leave.
-      bool drained = true;
-      for (int i = 0; drained && i < n_q; ++i) drained = mbar_wait(q_full(i), 0u, p.timeout_ns, nullptr);
-      for (int j = k_issued - 1; drained && j >= 0 && j >= k_issued - kAttnStages; --j) {
-        drained = mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
-      }
-      for (int j = v_issued - 1; drained && j >= 0 && j >= v_issued - kAttnStages; --j) {
-        drained = mbar_wait(v_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
-      }
-      if (!drained) attn_raise(p, abort_flag, kDevTimeoutDrain);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ---- MMA issuer ----------------------------------------------------------
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(kAttnBQ, kAttnBKV, false, false);  // Q (K-major) x K^T (K-major)
-      constexpr uint32_t idesc_o = idesc_bf16_f32(kAttnBQ, kAttnD, false, true);     // P (TMEM) x V (MN-major)
-      // 16-wide K slices: K-major operands step 32 B inside a 64-wide atom
-      // and 16 KiB between the two atoms; the MN-major V steps 16 keys =
-      // 2 KiB inside a 64-key half and 16 KiB between halves; P in TMEM
-      // steps 8 columns (16 bf16).
-      auto kmajor = [](uint32_t tile, int k) {
-        return smem_desc_sw128(tile + (uint32_t)((k >> 2) * 16384 + (k & 3) * 32), 16, 1024);
-      };
-      auto vdesc = [](uint32_t tile, int k) {
-        return smem_desc_sw128(tile + (uint32_t)((k >> 2) * 16384 + (k & 3) * 2048), 8192, 1024);
-      };
-      auto issue_s = [&](int i, int j) {
-        const uint32_t qa = sQ + (uint32_t)(i * Plan::kTileBytes);
-        const uint32_t kt = sK + (uint32_t)((j & 1) * Plan::kTileBytes);
-#pragma unroll
-        for (int k = 0; k < kAttnD / kUmmaK; ++k) {
-          umma_bf16(tmem_base + (uint32_t)(i * 128), kmajor(qa, k), kmajor(kt, k), idesc_s, k > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int i, int j) {
-        const uint32_t vt = sV + (uint32_t)((j & 1) * Plan::kTileBytes);
-#pragma unroll
-        for (int k = 0; k < kAttnBKV / kUmmaK; ++k) {
-          umma_bf16_ts(tmem_base + 256u + (uint32_t)(i * 128), tmem_base + (uint32_t)(i * 128 + k * 8),
-                       vdesc(vt, k), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-        }
-      };
-      auto wait_k = [&](int j) { return mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag); };
-      bool ok = true;
-      for (int i = 0; ok && i < n_q; ++i) ok = mbar_wait(q_full(i), 0u, p.timeout_ns, abort_flag);
-      if (ok && n_max > 0) {
-        ok = wait_k(0);
-        if (ok) {
-          tc_fence_after();
-          for (int i = 0; i < n_q; ++i) {
-            issue_s(i, 0);
-            umma_commit(s_full(i));
-          }
-          umma_commit(k_empty(0));
-        }
-      }
-      const int n_tiles[2] = {n0, n1};
-      for (int j = 0; j < n_max && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(v_full(s), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag)) {
-          ok = false;
-          break;
-        }
-        bool k_ready = false;
-#pragma unroll
-        for (int i = 0; i < kAttnQTiles; ++i) {
-          if (!ok || j >= n_tiles[i]) continue;
-          if (!mbar_wait(p_full(i), (uint32_t)j & 1u, p.timeout_ns, abort_flag)) {
+        bool ok = true;
+        int k_issued = 0, v_issued = 0;
+        for (int j = 0; j < n_max && ok; ++j) {
+          const int s = j & 1;
+          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+          if (!mbar_wait(k_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
             ok = false;
-            continue;
+            break;
           }
-          tc_fence_after();
-          issue_pv(i, j);
-          if (i == kAttnQTiles - 1 || j >= n_tiles[kAttnQTiles - 1]) umma_commit(v_empty(s));  // last user of V_j
-          if (j + 1 < n_tiles[i]) {
-            if (!k_ready) {
-              if (!wait_k(j + 1)) {
-                ok = false;
-                continue;
-              }
-              k_ready = true;
-              tc_fence_after();
+          mbar_arrive_expect_tx(k_full(s), Plan::kTileBytes);
+          for (int h = 0; h < 2; ++h) {
+            tma_load_3d(sK + s * Plan::kTileBytes + h * 16384, &tmK, k_full(s), kv_col0 + 64 * h, j * kAttnBKV, bat,
+                        pol_keep);
+          }
+          ++k_issued;
+          if (!mbar_wait(v_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(v_full(s), Plan::kTileBytes);
+          // V tile as two 64-key halves, each two 64-column atoms of [64 keys][64 d].
+          for (int hk = 0; hk < 2; ++hk) {
+            for (int h = 0; h < 2; ++h) {
+              tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + h * 8192, &tmV, v_full(s), kv_col0 + 64 * h,
+                          j * kAttnBKV + 64 * hk, bat, pol_keep);
             }
-            issue_s(i, j + 1);
-            umma_commit(s_full(i));
-          } else {
-            umma_commit(o_full(i));
+          }
+          ++v_issued;
+        }
+        if (!ok) attn_raise(p, abort_flag, kDevTimeoutProducer);
+        // Let the copies in flight land before the CTA can leave.
+        bool drained = true;
+        for (int i = 0; drained && i < n_q; ++i) drained = mbar_wait(q_full(i), 0u, p.timeout_ns, nullptr);
+        for (int j = k_issued - 1; drained && j >= 0 && j >= k_issued - kAttnStages; --j) {
+          drained = mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
+        }
+        for (int j = v_issued - 1; drained && j >= 0 && j >= v_issued - kAttnStages; --j) {
+          drained = mbar_wait(v_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
+        }
+        if (!drained) attn_raise(p, abort_flag, kDevTimeoutDrain);
+      }
+      __syncwarp();
+    } else if (warp == kAttnMmaWarp) {
+      // ---- MMA issuer ----------------------------------------------------------
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_bf16_f32(kAttnBQ, kAttnBKV, false, false);  // Q (K-major) x K^T (K-major)
+        constexpr uint32_t idesc_o = idesc_bf16_f32(kAttnBQ, kAttnD, false, true);     // P (TMEM) x V (MN-major)
+        // 16-wide K slices: K-major operands step 32 B inside a 64-wide atom
+        // and 16 KiB between the two atoms; the MN-major V steps 16 keys =
+        // 2 KiB inside a 64-key half and 16 KiB between halves; P in TMEM
+        // steps 8 columns (16 bf16).
+        auto kmajor = [](uint32_t tile, int k) {
+          return smem_desc_sw128(tile + (uint32_t)((k >> 2) * 16384 + (k & 3) * 32), 16, 1024);
+        };
+        auto vdesc = [](uint32_t tile, int k) {
+          return smem_desc_sw128(tile + (uint32_t)((k >> 2) * 16384 + (k & 3) * 2048), 8192, 1024);
+        };
+        auto issue_s = [&](int i, int j) {
+          const uint32_t qa = sQ + (uint32_t)(i * Plan::kTileBytes);
+          const uint32_t kt = sK + (uint32_t)((j & 1) * Plan::kTileBytes);
+  #pragma unroll
+          for (int k = 0; k < kAttnD / kUmmaK; ++k) {
+            umma_bf16(tmem_base + (uint32_t)(i * 128), kmajor(qa, k), kmajor(kt, k), idesc_s, k > 0 ? 1u : 0u);
+          }
+        };
+        auto issue_pv = [&](int i, int j) {
+          const uint32_t vt = sV + (uint32_t)((j & 1) * Plan::kTileBytes);
+  #pragma unroll
+          for (int k = 0; k < kAttnBKV / kUmmaK; ++k) {
+            umma_bf16_ts(tmem_base + 256u + (uint32_t)(i * 128), tmem_base + (uint32_t)(i * 128 + k * 8),
+                         vdesc(vt, k), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          }
+        };
+        auto wait_k = [&](int j) { return mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag); };
+        bool ok = true;
+        for (int i = 0; ok && i < n_q; ++i) ok = mbar_wait(q_full(i), 0u, p.timeout_ns, abort_flag);
+        if (ok && n_max > 0) {
+          ok = wait_k(0);
+          if (ok) {
+            tc_fence_after();
+            for (int i = 0; i < n_q; ++i) {
+              issue_s(i, 0);
+              umma_commit(s_full(i));
+            }
+            umma_commit(k_empty(0));
           }
         }
-        if (ok && j + 1 < n_max) umma_commit(k_empty((j + 1) & 1));
+        const int n_tiles[2] = {n0, n1};
+        for (int j = 0; j < n_max && ok; ++j) {
+          const int s = j & 1;
+          if (!mbar_wait(v_full(s), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          bool k_ready = false;
+  #pragma unroll
+          for (int i = 0; i < kAttnQTiles; ++i) {
+            if (!ok || j >= n_tiles[i]) continue;
+            if (!mbar_wait(p_full(i), (uint32_t)j & 1u, p.timeout_ns, abort_flag)) {
+              ok = false;
+              continue;
+            }
+            tc_fence_after();
+            issue_pv(i, j);
+            if (i == kAttnQTiles - 1 || j >= n_tiles[kAttnQTiles - 1]) umma_commit(v_empty(s));  // last user of V_j
+            if (j + 1 < n_tiles[i]) {
+              if (!k_ready) {
+                if (!wait_k(j + 1)) {
+                  ok = false;
+                  continue;
+                }
+                k_ready = true;
+                tc_fence_after();
+              }
+              issue_s(i, j + 1);
+              umma_commit(s_full(i));
+            } else {
+              umma_commit(o_full(i));
+            }
+          }
+          if (ok && j + 1 < n_max) umma_commit(k_empty((j + 1) & 1));
+        }
+        if (!ok) attn_raise(p, abort_flag, kDevTimeoutMma);
+        umma_commit(drain);
+        if (!mbar_wait(drain, 0u, p.timeout_ns, nullptr)) attn_raise(p, abort_flag, kDevTimeoutDrain);
       }
-      if (!ok) attn_raise(p, abort_flag, kDevTimeoutMma);
-      umma_commit(drain);
-      if (!mbar_wait(drain, 0u, p.timeout_ns, nullptr)) attn_raise(p, abort_flag, kDevTimeoutDrain);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
-    // ---- softmax + epilogue (warps 2..5: tile 0, warps 6..9: tile 1) ----------
-    const int tile = (warp - 2) >> 2;
+    setmaxnreg_inc<kAttnRegsSoftmax>();
+    // ---- softmax + epilogue (warps 0..3: tile 0, warps 4..7: tile 1) ----------
+    const int tile = warp >> 2;
     const int qw = warp & 3;                // TMEM lane quarter this warp may access
     const int row = qw * 32 + (int)lane;     // query row in the tile
     const int qt = qt0 + tile;
@@ -499,7 +519,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kAttnMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }

@@ -832,7 +832,8 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   if (head_dim != b200::kAttnD) return B200_ERR_INVALID_ARG;
   if ((heads > 0 && kv_heads == 0) || (kv_heads > 0 && heads % kv_heads != 0)) return B200_ERR_INVALID_ARG;
   if (batch == 0 || seq_len == 0 || heads == 0) return B200_OK;
-  if (batch > 65535 || heads > 65535 || seq_len > 0x7fffffffLL || heads * head_dim > 0x7fffffffLL)
+  if (batch > 65535 || heads > 65535 || heads * batch > 0x7fffffffLL || seq_len > 65535LL * 2 * b200::kAttnBQ ||
+      heads * head_dim > 0x7fffffffLL)
     return B200_ERR_TOO_LARGE;
   if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return B200_ERR_INVALID_ARG;
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return B200_ERR_ALIGNMENT;
@@ -861,8 +862,8 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3((unsigned)((p.num_q_tiles + b200::kAttnQTiles - 1) / b200::kAttnQTiles), (unsigned)heads,
-                     (unsigned)batch);
+  cfg.gridDim = dim3((unsigned)(heads * batch), (unsigned)((p.num_q_tiles + b200::kAttnQTiles - 1) / b200::kAttnQTiles),
+                     1);
   cfg.blockDim = dim3(b200::kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = b200::AttnSmemPlan::kAllocBytes;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream_);

@@ -311,6 +311,19 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// Register reallocation between warpgroups (all four warps of a warpgroup
+// execute it).  inc waits until enough registers are free in the CTA's pool,
+// which holds exactly (threads x registers per thread at launch): the shares
+// the warpgroups move to must add up to no more than that.
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // D (TMEM) (+)= A x B with the A operand read from tensor memory: row m of A
 // in TMEM lane m, two bf16 per 32-bit column (K-major), B from shared memory.
 __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
