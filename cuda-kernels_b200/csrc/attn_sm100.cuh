@@ -25,7 +25,7 @@
 //   warps 10,11 idle.
 // Softmax: one thread per query row (= TMEM lane) holds the row's 128 scores
 // in registers (the third warpgroup gives up registers with setmaxnreg so
-// that the softmax warpgroups have 224 each): S row from TMEM, running max and
+// that the softmax warpgroups have 208 each): S row from TMEM, running max and
 // sum in fp32 (exp2 domain), P row as bf16 back into TMEM; lazy rescaling —
 // the running max, and with it O in TMEM, is only moved when the row max grows
 // by more than 2^8 — and at the end O / l -> bf16 -> TMA store (staged in the
@@ -55,8 +55,8 @@ constexpr int kAttnProducerWarp = 4 * kAttnQTiles;
 constexpr int kAttnMmaWarp = kAttnProducerWarp + 1;
 // Registers per thread: at launch (the kernel is compiled to exactly this),
 // after reallocation for the producer/MMA warpgroup and for the softmax
-// warpgroups.  128 * 56 + 256 * 224 = 384 * 168.
-constexpr uint32_t kAttnRegsLaunch = 168, kAttnRegsOther = 56, kAttnRegsSoftmax = 224;
+// warpgroups.  128 * 88 + 256 * 208 = 384 * 168.
+constexpr uint32_t kAttnRegsLaunch = 168, kAttnRegsOther = 88, kAttnRegsSoftmax = 208;
 static_assert(128 * kAttnRegsOther + kAttnQTiles * 128 * kAttnRegsSoftmax <= kAttnThreads * kAttnRegsLaunch,
               "register reallocation exceeds the launch pool");
 // Every kAttnPolyEvery-th pair of exponentials on the FMA pipe (0: none).
@@ -81,8 +81,8 @@ struct AttnSmemPlan {
   static constexpr int kOffK = kOffQ + kAttnQTiles * kTileBytes;
   static constexpr int kOffV = kOffK + kAttnStages * kTileBytes;
   static constexpr int kOffBar = kOffV + kAttnStages * kTileBytes;
-  // q_full[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain
-  static constexpr int kNumBars = 3 * kAttnQTiles + 4 * kAttnStages + kAttnQTiles + 1;
+  // q_full[Q], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[Q], p_full[Q][2], o_full[Q], drain
+  static constexpr int kNumBars = 5 * kAttnQTiles + 4 * kAttnStages + 1;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAbort = kOffTmemHolder + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -128,20 +128,19 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// P = 2^(x * scale - m_use) for one row of 128 scores, packed as bf16 pairs
-// (key 2c in the low half of word c), and its sum.  kPoly: every
+// P = 2^(x * scale - m_use) for N scores of one row, packed as bf16 pairs
+// (key 2c in the low half of word c), and their sum.  kPoly: every
 // kAttnPolyEvery-th pair goes through poly_exp2x2 (only for tiles without
 // masked keys: there x = -inf must give exactly 0).
-template <bool kPoly>
-__device__ __forceinline__ float row_exp(const float (&x)[kAttnBKV], float scale, float m_use,
-                                         uint32_t (&pw)[2][32]) {
+template <int N, bool kPoly>
+__device__ __forceinline__ float row_exp(const float* x, float scale, float m_use, uint32_t (&pw)[N / 2]) {
   const float2 sc = make_float2(scale, scale);
   const float2 nm = make_float2(-m_use, -m_use);
   float2 acc[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
-  for (int c = 0; c < kAttnBKV; c += 2) {
+  for (int c = 0; c < N; c += 2) {
     const float2 t = __ffma2_rn(make_float2(x[c], x[c + 1]), sc, nm);
     float2 e;
     if (kPoly && kAttnPolyEvery > 0 && ((c >> 1) % (kAttnPolyEvery > 0 ? kAttnPolyEvery : 1)) == kAttnPolyEvery - 1) {
@@ -150,7 +149,7 @@ __device__ __forceinline__ float row_exp(const float (&x)[kAttnBKV], float scale
       e = make_float2(fast_exp2(t.x), fast_exp2(t.y));
     }
     acc[(c >> 1) & 3] = __fadd2_rn(acc[(c >> 1) & 3], e);
-    pw[c >> 6][(c >> 1) & 31] = pack_bf16x2(e.x, e.y);
+    pw[c >> 1] = pack_bf16x2(e.x, e.y);
   }
   const float2 s01 = __fadd2_rn(acc[0], acc[1]);
   const float2 s23 = __fadd2_rn(acc[2], acc[3]);
@@ -188,9 +187,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto v_full = [&](int s) { return bar0 + 8u * (kAttnQTiles + 2 * kAttnStages + s); };
   auto v_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + 3 * kAttnStages + s); };
   auto s_full = [&](int i) { return bar0 + 8u * (kAttnQTiles + 4 * kAttnStages + i); };
-  auto p_full = [&](int i) { return bar0 + 8u * (2 * kAttnQTiles + 4 * kAttnStages + i); };
-  auto o_full = [&](int i) { return bar0 + 8u * (3 * kAttnQTiles + 4 * kAttnStages + i); };
-  const uint32_t drain = bar0 + 8u * (4 * kAttnQTiles + 4 * kAttnStages);  // every MMA issued has completed
+  // P of tile i, keys 64 h .. 64 h + 63, in TMEM.
+  auto p_full = [&](int i, int h) { return bar0 + 8u * (2 * kAttnQTiles + 4 * kAttnStages + 2 * i + h); };
+  auto o_full = [&](int i) { return bar0 + 8u * (4 * kAttnQTiles + 4 * kAttnStages + i); };
+  const uint32_t drain = bar0 + 8u * (5 * kAttnQTiles + 4 * kAttnStages);  // every MMA issued has completed
   volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
 
@@ -216,7 +216,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; i < kAttnQTiles; ++i) {
       mbar_init(q_full(i), 1);
       mbar_init(s_full(i), 1);
-      mbar_init(p_full(i), 4);
+      mbar_init(p_full(i, 0), 4);
+      mbar_init(p_full(i, 1), 4);
       mbar_init(o_full(i), 1);
     }
     for (int s = 0; s < kAttnStages; ++s) {
@@ -318,15 +319,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         auto issue_s = [&](int i, int j) {
           const uint32_t qa = sQ + (uint32_t)(i * Plan::kTileBytes);
           const uint32_t kt = sK + (uint32_t)((j & 1) * Plan::kTileBytes);
-  #pragma unroll
+#pragma unroll
           for (int k = 0; k < kAttnD / kUmmaK; ++k) {
             umma_bf16(tmem_base + (uint32_t)(i * 128), kmajor(qa, k), kmajor(kt, k), idesc_s, k > 0 ? 1u : 0u);
           }
         };
-        auto issue_pv = [&](int i, int j) {
+        // Keys 64 h .. 64 h + 63 of P V (K slices 4 h .. 4 h + 3).
+        auto issue_pv = [&](int i, int j, int h) {
           const uint32_t vt = sV + (uint32_t)((j & 1) * Plan::kTileBytes);
-  #pragma unroll
-          for (int k = 0; k < kAttnBKV / kUmmaK; ++k) {
+#pragma unroll
+          for (int k = 4 * h; k < 4 * h + 4; ++k) {
             umma_bf16_ts(tmem_base + 256u + (uint32_t)(i * 128), tmem_base + (uint32_t)(i * 128 + k * 8),
                          vdesc(vt, k), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
           }
@@ -353,15 +355,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             break;
           }
           bool k_ready = false;
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < kAttnQTiles; ++i) {
             if (!ok || j >= n_tiles[i]) continue;
-            if (!mbar_wait(p_full(i), (uint32_t)j & 1u, p.timeout_ns, abort_flag)) {
+            // The first half of P V starts while the softmax still works on
+            // the second half of the row.
+            if (!mbar_wait(p_full(i, 0), (uint32_t)j & 1u, p.timeout_ns, abort_flag)) {
               ok = false;
               continue;
             }
             tc_fence_after();
-            issue_pv(i, j);
+            issue_pv(i, j, 0);
+            if (!mbar_wait(p_full(i, 1), (uint32_t)j & 1u, p.timeout_ns, abort_flag)) {
+              ok = false;
+              continue;
+            }
+            tc_fence_after();
+            issue_pv(i, j, 1);
             if (i == kAttnQTiles - 1 || j >= n_tiles[kAttnQTiles - 1]) umma_commit(v_empty(s));  // last user of V_j
             if (j + 1 < n_tiles[i]) {
               if (!k_ready) {
@@ -447,8 +457,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float factor = (move && m != -INFINITY) ? fast_exp2(m - m_new) : 1.0f;
       const float m_next = move ? m_new : m;
       const float m_use = (m_next == -INFINITY) ? 0.0f : m_next;
-      uint32_t pw[2][32];
-      const float sum = masked ? row_exp<false>(x, p.scale_log2, m_use, pw) : row_exp<true>(x, p.scale_log2, m_use, pw);
       if (j > 0 && __any_sync(0xffffffffu, move && factor != 1.0f)) {
         // S_i(j) was issued after P_i(j-1) V(j-1), and its completion signal
         // covers that product: O is stable until this warpgroup's P is in.
@@ -467,14 +475,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l *= factor;
         m = m_new;
       }
-      l += sum;
-      // P row -> TMEM over the first 64 columns of S (two bf16 per column).
-      tmem_st_32x32b_x32(tS, pw[0]);
-      tmem_st_32x32b_x32(tS + 32u, pw[1]);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(tile));
+      // P row -> TMEM over the first 64 columns of S (two bf16 per column),
+      // in two halves of 64 keys, each published as soon as it is stored.
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pw[32];
+        l += masked ? row_exp<64, false>(x + 64 * h, p.scale_log2, m_use, pw)
+                    : row_exp<64, true>(x + 64 * h, p.scale_log2, m_use, pw);
+        tmem_st_32x32b_x32(tS + (uint32_t)(32 * h), pw);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(tile, h));
+      }
     }
     if (!ok) {
       if (lane == 0) attn_raise(p, abort_flag, kDevTimeoutEpilogue);

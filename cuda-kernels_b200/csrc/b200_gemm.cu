@@ -77,6 +77,10 @@ struct DeviceState {
   uint32_t* status_ptr = nullptr;
   uint64_t timeout_ns = kDefaultTimeoutNs;
   std::atomic<uint32_t> epoch{0};  // split-K hand-off counter, one step per launch
+  // The attention kernel moves registers between warpgroups (setmaxnreg); its
+  // shares add up to exactly the pool of a launch at kAttnRegsLaunch
+  // registers per thread, so it only runs when the binary has that count.
+  bool attn_regs_ok = false;
 };
 
 // Split-K plan for the pair kernel's last, partial wave of tiles (see
@@ -199,6 +203,11 @@ int init_device(int dev, DeviceState& st) {
   if (cudaFuncSetAttribute(b200::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            b200::AttnSmemPlan::kAllocBytes) != cudaSuccess)
     return B200_ERR_CUDA;
+  {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, b200::flash_attn_fwd_kernel) != cudaSuccess) return B200_ERR_CUDA;
+    st.attn_regs_ok = fa.numRegs == (int)b200::kAttnRegsLaunch;
+  }
   if (set_skinny_attrs<16>() != B200_OK || set_skinny_attrs<32>() != B200_OK || set_skinny_attrs<64>() != B200_OK ||
       set_skinny_attrs<128>() != B200_OK)
     return B200_ERR_CUDA;
@@ -840,6 +849,7 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   DeviceState* st = nullptr;
   int rc = current_device_state(&st);
   if (rc != B200_OK) return rc;
+  if (!st->attn_regs_ok) return B200_ERR_CUDA;  // built with another register count: never launch it
   const uint64_t cols = (uint64_t)(heads * head_dim);
   const uint64_t kv_cols = (uint64_t)(kv_heads * head_dim);
   CUtensorMap tmQ, tmK, tmV, tmO;
