@@ -437,8 +437,9 @@ def run_fp32(args) -> int:
 def run_attention(args) -> int:
     """--attention: the reference's flash_attn benchmark (flash_attn/main.py:28-56,
     README.md:9): causal bf16 attention, (batch, seq, heads, head_dim) = (1, S, 32, 128),
-    S = 512 ... 8192; ours against torch SDPA and the flash-attn package on the same GPU.
-    TFLOPS counted as the reference does for causal attention: 2 * 2 * B * H * S^2 * D / 2."""
+    S = 512 ... 8192, plus the full (non-causal) mask at 4096 and 8192; ours against torch
+    SDPA and the flash-attn package on the same GPU.  TFLOPS counted as the reference does:
+    2 * 2 * B * H * S^2 * D, halved for the causal mask."""
     import torch
     import torch.nn.functional as F
     torch.cuda.set_device(0)
@@ -448,22 +449,28 @@ def run_attention(args) -> int:
         from flash_attn import flash_attn_func
     except Exception:  # noqa: BLE001 - the comparison is optional
         flash_attn_func = None
-    for S in (512, 1024, 2048, 4096, 8192):
+    peaks = _peaks()
+    cases = [(S, True) for S in (512, 1024, 2048, 4096, 8192)] + [(4096, False), (8192, False)]
+    for S, causal in cases:
         g = torch.Generator(device=dev).manual_seed(S)
         q, k, v = (torch.randn((1, S, 32, 128), generator=g, device=dev).bfloat16() for _ in range(3))
         qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         out = torch.empty_like(q)
-        fns = {"b200": lambda i: b200_gemm.flash_attn(q, k, v, causal=True, out=out),
-               "torch_sdpa": lambda i: F.scaled_dot_product_attention(qt, kt, vt, is_causal=True)}
+        fns = {"b200": lambda i: b200_gemm.flash_attn(q, k, v, causal=causal, out=out),
+               "torch_sdpa": lambda i: F.scaled_dot_product_attention(qt, kt, vt, is_causal=causal)}
         if flash_attn_func is not None:
-            fns["flash_attn_pkg"] = lambda i: flash_attn_func(q, k, v, causal=True)
+            fns["flash_attn_pkg"] = lambda i: flash_attn_func(q, k, v, causal=causal)
         t = _time_variants(fns, target_ms=args.target_ms)
         b200_gemm.check_status()
-        flops = 2.0 * 2.0 * 32 * S * S * 128 / 2.0
-        print(json.dumps({"what": "flash_attention_causal", "config": {"batch": 1, "seq_len": S, "heads": 32,
-                                                                        "head_dim": 128, "dtype": "bf16"},
-                          "ms": {k_: round(v_, 4) for k_, v_ in t.items()},
-                          "tflops": {k_: round(flops / (v_ / 1e3) / 1e12, 1) for k_, v_ in t.items()}}),
+        flops = 2.0 * 2.0 * 32 * S * S * 128 / (2.0 if causal else 1.0)
+        tf = {k_: round(flops / (v_ / 1e3) / 1e12, 1) for k_, v_ in t.items()}
+        print(json.dumps({"what": "flash_attention_" + ("causal" if causal else "full"),
+                          "config": {"batch": 1, "seq_len": S, "heads": 32, "head_dim": 128, "dtype": "bf16"},
+                          "ms": {k_: round(v_, 4) for k_, v_ in t.items()}, "tflops": tf,
+                          # each size is timed in a ~0.25 s loop: the sustained (power-capped) peak applies
+                          "roofline": {"bound": "tensor", "achieved": tf["b200"], "peak": peaks["sustained"],
+                                       "unit": "TFLOP/s", "frac": round(tf["b200"] / peaks["sustained"], 3),
+                                       "peak_source": peaks["source"]}}),
               flush=True)
     return 0
 
