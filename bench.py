@@ -178,6 +178,32 @@ def cpu_baseline(target_s: float = 10.0, rows: int = 512):
                       f"(oracle/gemm_oracle.c, fp32 accumulate, {dt:.1f} s)"}
 
 
+def attention_cpu_baseline(target_s: float = 3.0, seq: int = 2048):
+    """The attention oracle (exact fp64 attention in numpy, oracle/oracle.py) on the
+    host cores: one head of the causal benchmark shape, repeated for ~target_s."""
+    import numpy as np
+    from oracle import oracle as o
+    rng = np.random.default_rng(2)
+    q, k, v = (o.f32_to_bf16(rng.standard_normal((1, seq, 1, 128)).astype(np.float32)) for _ in range(3))
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([int(i.get("num_threads", 1)) for i in threadpool_info()] or [1])
+    except Exception:  # noqa: BLE001 - the thread count is informational
+        cores = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        o.attention(q, k, v, True)
+        n += 1
+        if time.perf_counter() - t0 >= target_s:
+            break
+    dt = time.perf_counter() - t0
+    tflops = 2.0 * 2.0 * seq * seq * 128 / 2.0 * n / dt / 1e12
+    return {"value": round(tflops, 5), "unit": "TFLOPS", "cores": cores, "kind": "port",
+            "sample": f"{n} x causal attention batch 1, seq {seq}, 1 head, head_dim 128 "
+                      f"(oracle.attention, fp64 numpy, {dt:.1f} s)"}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference arithmetic on the host cores (oracle port)."""
     if rank != 0:
@@ -450,6 +476,7 @@ def run_attention(args) -> int:
     except Exception:  # noqa: BLE001 - the comparison is optional
         flash_attn_func = None
     peaks = _peaks()
+    cpu = None if args.no_cpu_baseline else attention_cpu_baseline()
     cases = [(S, True) for S in (512, 1024, 2048, 4096, 8192)] + [(4096, False), (8192, False)]
     for S, causal in cases:
         g = torch.Generator(device=dev).manual_seed(S)
@@ -470,7 +497,8 @@ def run_attention(args) -> int:
                           # each size is timed in a ~0.25 s loop: the sustained (power-capped) peak applies
                           "roofline": {"bound": "tensor", "achieved": tf["b200"], "peak": peaks["sustained"],
                                        "unit": "TFLOP/s", "frac": round(tf["b200"] / peaks["sustained"], 3),
-                                       "peak_source": peaks["source"]}}),
+                                       "peak_source": peaks["source"]},
+                          "cpu_baseline": cpu}),
               flush=True)
     return 0
 
