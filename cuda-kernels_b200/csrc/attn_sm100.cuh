@@ -19,14 +19,16 @@
 //                                   read from TMEM, where the softmax wrote it
 //                                   (bf16) over S_i, B = the V tile in its
 //                                   natural [key][d] layout (an MN-major operand);
-//               issued in the order P_0 V_j, S_0 (j+1), P_1 V_j, S_1 (j+1), so
+//               issued in the order P_0 V_j, S_0 (j+1), P_1 V_j, S_1 (j+1)
+//               (P V as two halves of 64 keys, each after its half of P), so
 //               that each softmax warpgroup works while the tensor cores run
 //               the other tile's two products;
 //   warps 10,11 idle.
 // Softmax: one thread per query row (= TMEM lane) holds the row's 128 scores
 // in registers (the third warpgroup gives up registers with setmaxnreg so
 // that the softmax warpgroups have 208 each): S row from TMEM, running max and
-// sum in fp32 (exp2 domain), P row as bf16 back into TMEM; lazy rescaling —
+// sum in fp32 (exp2 domain), P row as bf16 back into TMEM in two 64-key
+// halves (the first half of P V starts while the second is computed); lazy rescaling —
 // the running max, and with it O in TMEM, is only moved when the row max grows
 // by more than 2^8 — and at the end O / l -> bf16 -> TMA store (staged in the
 // tile's Q buffer).
