@@ -34,7 +34,8 @@ def _inputs(B, S, H, seed, grow=False, Hkv=None):
 
 
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("shape", [(1, 128, 2), (2, 384, 3), (1, 200, 2), (1, 1024, 4), (1, 77, 1)],
+@pytest.mark.parametrize("shape", [(1, 128, 2), (2, 384, 3), (1, 200, 2), (1, 1024, 4), (1, 77, 1), (1, 1, 2),
+                                   (3, 130, 5)],
                          ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("grow", [False, True])
 def test_attention_vs_exact(shape, causal, grow):
