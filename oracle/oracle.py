@@ -27,6 +27,9 @@ def build() -> None:
     """Compile the C oracle (gcc) and, when the reference checkout is present, oracle/_ref."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
     subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    from oracle import build_ref_fa2  # the reference's attention operator, when its sources are present
+
+    build_ref_fa2.build()
 
 
 def _load():

@@ -8,6 +8,8 @@ batches and heads, grouped-query attention (fewer key/value heads than query
 heads, as the reference's kernel allows), the reference-shaped torch binding
 (fa2_tma_lazy_rescale), and scores that grow along the keys so the lazy
 rescaling of the running max is exercised."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -15,7 +17,7 @@ import torch.nn.functional as F
 
 import b200_gemm
 from oracle import oracle as o
-from tests._util import bits
+from tests._util import bits, from_bits
 
 pytestmark = pytest.mark.gpu
 
@@ -95,6 +97,47 @@ def test_reference_binding_matches_c_abi():
     # strided tensor maps accept them.
     qt = q.transpose(1, 2).contiguous().transpose(1, 2)
     assert torch.equal(ext.fa2_tma_lazy_rescale(qt, k, v), o_ext)
+
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("name", ["fa2_1x128x2_mha", "fa2_1x192x4_gqa2", "fa2_2x256x2_mha"])
+def test_attention_vs_reference_golden(name):
+    """Against the reference operator's own outputs (fa2_tma_lazy_rescale run on a
+    B200, tests/golden/make_golden_attn.py): within the reference's check, and no
+    less accurate than the reference against the exact result."""
+    d = np.load(os.path.join(GOLDEN, name + ".npz"))
+    q, k, v = (from_bits(d[x]).to(DEV) for x in ("Q", "K", "V"))
+    out = b200_gemm.flash_attn(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    got = out.float().cpu().numpy().astype(np.float64)
+    ref = o.bf16_to_f32(d["O_ref_fa2"]).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= 1e-2 + 1e-2 * np.abs(ref)), f"{name}: max {np.abs(got - ref).max():.4f}"
+    exact = o.attention(d["Q"], d["K"], d["V"], True)
+    ours, theirs = np.abs(got - exact).mean(), np.abs(ref - exact).mean()
+    assert ours <= 1.5 * theirs + 1e-4, f"{name}: mean error {ours:.2e} vs the reference's {theirs:.2e}"
+
+
+def test_attention_vs_reference_live():
+    """Against the reference operator run live (oracle/_ref/ref_fa2.so, built from
+    its own sources for sm_100a) on the benchmark's head layout with grouped heads."""
+    path = os.path.join(os.path.dirname(GOLDEN), "..", "oracle", "_ref", "ref_fa2.so")
+    if not os.path.exists(path):
+        pytest.skip("oracle/_ref/ref_fa2.so not built (needs the reference sources)")
+    from oracle import build_ref_fa2
+    ref_mod = build_ref_fa2.load()
+    q, k, v = (t.to(DEV) for t in _inputs(1, 1024, 8, seed=31, Hkv=2))
+    ours = b200_gemm.flash_attn(q, k, v, causal=True)
+    ref = ref_mod.fa2_tma_lazy_rescale(q, k, v)
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    torch.testing.assert_close(ours, ref, rtol=1e-2, atol=1e-2)
+    exact = o.attention(bits(q), bits(k), bits(v), True)
+    e_ours = np.abs(ours.float().cpu().numpy() - exact).mean()
+    e_ref = np.abs(ref.float().cpu().numpy() - exact).mean()
+    assert e_ours <= 1.5 * e_ref + 1e-4, f"mean error {e_ours:.2e} vs the reference's {e_ref:.2e}"
 
 
 def test_attention_large_vs_sdpa():
