@@ -18,6 +18,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_v8_tuned.so")
+REF_F32_LIB_PATH = os.path.join(HERE, "_ref", "libref_f32.so")
 
 _lib = None
 _ref = None
@@ -231,3 +232,23 @@ def ref_lib():
         lib.ref_matmul_v8_tuned.restype = ctypes.c_int
         _ref = lib
     return _ref
+
+
+_ref_f32 = None
+
+
+def ref_f32_available() -> bool:
+    return os.path.exists(REF_F32_LIB_PATH)
+
+
+def ref_f32_lib():
+    """ctypes handle of oracle/_ref/libref_f32.so: the reference's fp32 kernels
+    (fp32_matmul/matmul.cu, v1 :18-36 and v5 :231-325) rebuilt for sm_100a."""
+    global _ref_f32
+    if _ref_f32 is None:
+        lib = ctypes.CDLL(REF_F32_LIB_PATH)
+        for f in (lib.ref_matmul_f32_v1, lib.ref_matmul_f32_v5):
+            f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+            f.restype = ctypes.c_int
+        _ref_f32 = lib
+    return _ref_f32

@@ -12,6 +12,8 @@ tensor cores' fp32 accumulation, which over K' = 6K steps is not a
 round-to-nearest FMA chain; the errors stay around 1e-6 relative (TF32 would
 be ~1e-3, bf16 ~4e-3).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -92,3 +94,48 @@ def test_f32_k_zero_and_empty():
     torch.cuda.synchronize()
     assert torch.equal(c, torch.zeros((5, 7), device=DEV))
     assert b200_gemm.gemm_f32(torch.zeros((0, 4), device=DEV), torch.zeros((4, 3), device=DEV)).shape == (0, 3)
+
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("name", ["f32_37x53x301", "f32_128x128x256", "f32_256x128x96"])
+def test_f32_vs_reference_golden(name):
+    """Against the reference's own fp32 kernel outputs (v1, run on a B200 by
+    tests/golden/make_golden_f32.py): as accurate as they are, by the bar above."""
+    d = np.load(os.path.join(GOLDEN, name + ".npz"))
+    a, b = d["A"], d["B"]
+    c = b200_gemm.gemm_f32(torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV), b_layout="kn")
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    exact, _ = o.gemm_f32_f64(a, b, 1)
+    ours, ref = _errors(c.cpu().numpy(), exact), _errors(d["C_ref_v1"], exact)
+    ctx = f"{name}: ours {ours}, reference v1 {ref}"
+    assert ours[0] <= 4.0 * ref[0] and ours[1] <= 5.0 * ref[1] and ours[1] < 1e-5, ctx
+
+
+def test_f32_vs_reference_live():
+    """Against the reference's fp32 kernels run live (oracle/_ref/libref_f32.so) on
+    its benchmark layout at 512 x 1024 x 768: v1 and its best kernel, v5."""
+    if not o.ref_f32_available():
+        pytest.skip("oracle/_ref/libref_f32.so not built (needs the reference sources)")
+    lib = o.ref_f32_lib()
+    M, N, K = 512, 1024, 768
+    g = torch.Generator().manual_seed(5)
+    a, b = torch.randn((M, K), generator=g).to(DEV), torch.randn((K, N), generator=g).to(DEV)
+    ours = b200_gemm.gemm_f32(a, b, b_layout="kn")
+    outs = {}
+    for v, f in (("v1", lib.ref_matmul_f32_v1), ("v5", lib.ref_matmul_f32_v5)):
+        c = torch.empty((M, N), device=DEV)
+        torch.cuda.synchronize()
+        assert f(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K) == 0
+        torch.cuda.synchronize()
+        outs[v] = c.cpu().numpy()
+    assert b200_gemm.check_status() == 0
+    exact, _ = o.gemm_f32_f64(a.cpu().numpy(), b.cpu().numpy(), 1)
+    e = _errors(ours.cpu().numpy(), exact)
+    # The CPU restatement is the reference's v1 bit for bit.
+    assert np.array_equal(outs["v1"], o.gemm_f32(a.cpu().numpy(), b.cpu().numpy(), 1))
+    for v in ("v1", "v5"):
+        r = _errors(outs[v], exact)
+        assert e[0] <= 4.0 * r[0] and e[1] <= 5.0 * r[1], f"ours {e} vs reference {v} {r}"

@@ -85,6 +85,24 @@ def test_attention_oracle_pinned_to_reference_kernel(name):
     assert same > 0.6, f"{name}: only {same:.2%} of elements equal"
 
 
+@pytest.mark.parametrize("name", ["f32_37x53x301", "f32_128x128x256", "f32_256x128x96"])
+def test_f32_oracle_pinned_to_reference_kernel(name):
+    """The fp32 restatement reproduces, bit for bit, the reference's fp32 v1 kernel
+    (one fp32 multiply-add chain per output over k in order, fp32_matmul/matmul.cu:18-36)
+    as run on a B200 by tests/golden/make_golden_f32.py; the reference's v5 and
+    cuBLAS agree with it within the classical fp32 dot-product bound."""
+    d = np.load(os.path.join(GOLDEN, name + ".npz"))
+    a, b = d["A"], d["B"]
+    c = o.gemm_f32(a, b, 1)
+    assert np.array_equal(c.view(np.uint32), d["C_ref_v1"].view(np.uint32)), \
+        f"{name}: {np.mean(c != d['C_ref_v1']):.3%} of elements differ from the reference's v1"
+    exact, absc = o.gemm_f32_f64(a, b, 1)
+    bound = a.shape[1] * 2.0 ** -24 * absc
+    for key in ("C_cublas", "C_ref_v5"):
+        if key in d.files:
+            assert np.all(np.abs(d[key].astype(np.float64) - exact) <= bound), f"{name}: {key} outside the bound"
+
+
 def test_attention_grouped_heads_match_repeated_heads():
     # heads = 4, kv_heads = 2: query heads 0, 1 use key/value head 0 and 2, 3 use
     # head 1 (fa2_tma_lazy_rescale.cu:113-114), i.e. plain attention with each
