@@ -72,6 +72,10 @@ struct AttnParams {
   int32_t group;  // heads / kv_heads: query heads per key/value head
   int32_t num_q_tiles;
   uint32_t causal;
+  // Query tiles of CTA row y: 0 -> (2 (Y-1-y), 2 (Y-1-y) + 1), the longest
+  // rows first; 1 -> (y, T-1-y), a short and a long causal row together, so
+  // that every CTA carries the same work (used when the grid is one wave).
+  uint32_t balanced;
   float scale_log2;  // log2(e) / sqrt(D): scores go straight to the exp2 domain
   uint64_t timeout_ns;
   uint32_t* status;
@@ -198,7 +202,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
-  const int qt0 = kAttnQTiles * ((int)gridDim.y - 1 - (int)blockIdx.y);  // first query tile of the CTA
+  // The CTA's two query tiles: qt_of[1] >= qt_of[0] + 1 (or past the end).
+  int qt_of[kAttnQTiles];
+  if (p.balanced) {
+    qt_of[0] = (int)blockIdx.y;
+    qt_of[1] = p.num_q_tiles - 1 - (int)blockIdx.y;
+    if (qt_of[1] <= qt_of[0]) qt_of[1] = p.num_q_tiles;  // the middle tile of an odd count stays alone
+  } else {
+    qt_of[0] = kAttnQTiles * ((int)gridDim.y - 1 - (int)blockIdx.y);
+    qt_of[1] = qt_of[0] + 1;
+  }
   const int head = (int)blockIdx.x % p.heads;
   const int bat = (int)blockIdx.x / p.heads;
   const int kv_tiles_all = (p.seq_len + kAttnBKV - 1) / kAttnBKV;
@@ -207,8 +220,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto kv_tiles = [&](int qt) {
     return qt >= p.num_q_tiles ? 0 : (p.causal ? min(qt + 1, kv_tiles_all) : kv_tiles_all);
   };
-  const int n0 = kv_tiles(qt0);
-  const int n1 = kv_tiles(qt0 + 1);  // >= n0, or 0
+  const int n0 = kv_tiles(qt_of[0]);
+  const int n1 = kv_tiles(qt_of[1]);  // >= n0, or 0
   const int n_max = max(n0, n1);
   const int n_q = n1 > 0 ? 2 : 1;    // query tiles this CTA holds
   const int col0 = head * kAttnD;                  // column of this head in the [seq, heads * D] view
@@ -258,7 +271,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mbar_arrive_expect_tx(q_full(i), Plan::kTileBytes);
           for (int h = 0; h < 2; ++h) {
             tma_load_3d(sQ + i * Plan::kTileBytes + h * 16384, &tmQ, q_full(i), col0 + 64 * h,
-                        (qt0 + i) * kAttnBQ, bat, pol_once);
+                        qt_of[i] * kAttnBQ, bat, pol_once);
           }
         }
         bool ok = true;
@@ -404,7 +417,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int tile = warp >> 2;
     const int qw = warp & 3;                // TMEM lane quarter this warp may access
     const int row = qw * 32 + (int)lane;     // query row in the tile
-    const int qt = qt0 + tile;
+    const int qt = qt_of[tile];
     const int n_kv = tile == 0 ? n0 : n1;
     const int q_idx = qt * kAttnBQ + row;    // query position
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;

@@ -865,6 +865,13 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   p.group = (int32_t)(heads / kv_heads);
   p.num_q_tiles = (int32_t)((seq_len + b200::kAttnBQ - 1) / b200::kAttnBQ);
   p.causal = causal ? 1u : 0u;
+  {
+    // With a causal mask, pairing a short row with a long one evens out the
+    // CTAs' work; that only pays while the whole grid runs in one wave (with
+    // more waves, longest-first order balances the SMs better).
+    const int64_t pairs = (p.num_q_tiles + b200::kAttnQTiles - 1) / b200::kAttnQTiles;
+    p.balanced = (causal && p.num_q_tiles > 2 && pairs * heads * batch <= st->sm_count) ? 1u : 0u;
+  }
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
   p.timeout_ns = st->timeout_ns;
   p.status = st->status_ptr;
