@@ -5,23 +5,33 @@ M=N=K=4096 and its fraction of the B200 dense BF16 peak; 1/2/4/8-GPU scaling.
 
 One step = one GEMM C = A @ B (A [4096,4096], B [4096,4096] row-major = the
 BASELINE config, U(-1,1) bf16) on each GPU.  With N GPUs (torchrun, one rank
-per GPU) the job is the row-sharded GEMM of the BASELINE: A [4096*N, 4096]
-split into one 4096-row panel per rank, B broadcast once from rank 0 over
-NCCL, C left sharded, so per-GPU work is fixed as N grows ("weak" scaling).
+per GPU) A is [4096*N, 4096], one 4096-row panel per rank; every step rank 0
+broadcasts B to all ranks over NCCL and each rank multiplies its panel, C
+stays sharded: per-GPU work is fixed as N grows ("weak" scaling) and the
+broadcast is inside every step.
 
 Timing: CUDA events on the launching stream, W warm-up steps, then exactly K
 timed steps bracketed by barrier + synchronize, max over ranks.  Inputs
 rotate over 4 buffer sets (4 x 96 MiB > 126 MB L2) so no step finds its
 operands in L2.  Clocks are sampled through NVML during the timed region.
 
-`e2e` repeats the step through the public API with host (pinned) buffers:
-host->device copy of the step's A (and of B by rank 0, then NCCL broadcast),
-the GEMM, and the device->host copy of C, all inside the timed region,
-pipelined over three streams as a serving loop would run it.
+The line also carries:
+  e2e        the step through the public API with host (pinned) buffers:
+             host->device copies of the step's inputs, the GEMM and the
+             device->host copy of C inside the timed region;
+  rowshard   BASELINE config 5 (131072x8192x8192 split over the N ranks, B
+             broadcast, C sharded; strong scaling), with the 1-GPU time of
+             the same job measured in the same run at N>1;
+  parity     (N>1) the sharded result on sampled rows against an fp32 CPU
+             product, and the fused all-gather GEMM against GEMM + NCCL
+             all-gather, bit for bit on every rank;
+  configs    (N=1) BASELINE configs 2-4, ours and cuBLAS in the same loop;
+  cpu_baseline  (N=1) the reference arithmetic on the host cores.
 
 `--impl reference` times the reference's arithmetic on the host cores (the
 reference has no CPU implementation of its own; this is the oracle port in
-oracle/gemm_oracle.c) on a bounded row sample of the same workload.
+oracle/gemm_oracle.c) on a bounded row sample of the same workload, on every
+host thread the process may use.
 """
 from __future__ import annotations
 
@@ -37,6 +47,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "cuda-kernels_b200"))
 sys.path.insert(0, REPO)
 
+METRIC = "bf16_gemm_tflops_4096"
 M_PER_RANK = 4096
 N_DIM = 4096
 K_DIM = 4096
@@ -155,27 +166,38 @@ def _max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def host_threads() -> int:
+    """Host threads the CPU legs use: every core this process may run on.  Set
+    explicitly (not inherited from OMP_NUM_THREADS, which torchrun sets to 1),
+    so the CPU figures do not change with the number of GPU ranks."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:  # not Linux
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(target_s: float = 10.0, rows: int = 512):
     """The oracle (CPU restatement of the reference arithmetic) on the host
     cores, on row panels of the same workload, repeated for ~target_s."""
     import numpy as np
     from oracle import oracle as o
+    threads = host_threads()
     rng = np.random.default_rng(0)
     a = o.f32_to_bf16(rng.uniform(-1, 1, (rows, K_DIM)).astype(np.float32))
     b = o.f32_to_bf16(rng.uniform(-1, 1, (K_DIM, N_DIM)).astype(np.float32))
-    o.gemm_f32acc(a[:8], b, 1)  # warm
+    o.gemm_f32acc(a[:8], b, 1, threads)  # warm
     t0 = time.perf_counter()
     n = 0
     while True:
-        o.gemm_bf16(a, b, 1)
+        o.gemm_bf16(a, b, 1, threads)
         n += 1
         if time.perf_counter() - t0 >= target_s:
             break
     dt = time.perf_counter() - t0
     tflops = 2.0 * rows * N_DIM * K_DIM * n / dt / 1e12
-    return {"value": round(tflops, 5), "unit": "TFLOPS", "cores": o.num_threads(), "kind": "port",
+    return {"value": round(tflops, 5), "unit": "TFLOPS", "cores": threads, "kind": "port",
             "sample": f"{n} x A[{rows},{K_DIM}] @ B[{K_DIM},{N_DIM}] row panels of the 4096^3 GEMM "
-                      f"(oracle/gemm_oracle.c, fp32 accumulate, {dt:.1f} s)"}
+                      f"(oracle/gemm_oracle.c, fp32 accumulate, {threads} threads, {dt:.1f} s)"}
 
 
 def attention_cpu_baseline(target_s: float = 3.0, seq: int = 2048):
@@ -205,32 +227,33 @@ def attention_cpu_baseline(target_s: float = 3.0, seq: int = 2048):
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference arithmetic on the host cores (oracle port)."""
+    """--impl reference: the reference arithmetic on the host cores (oracle port),
+    on every host thread this process may use, whatever the number of ranks."""
     if rank != 0:
         return 0
     import numpy as np
     from oracle import oracle as o
+    threads = host_threads()
     rows = args.ref_rows
     rng = np.random.default_rng(1)
     a = o.f32_to_bf16(rng.uniform(-1, 1, (rows, K_DIM)).astype(np.float32))
     b = o.f32_to_bf16(rng.uniform(-1, 1, (K_DIM, N_DIM)).astype(np.float32))
     for _ in range(args.warmup):
-        o.gemm_bf16(a, b, 1)
+        o.gemm_bf16(a, b, 1, threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        o.gemm_bf16(a, b, 1)
+        o.gemm_bf16(a, b, 1, threads)
     dt = time.perf_counter() - t0
     tflops = 2.0 * rows * N_DIM * K_DIM * args.steps / dt / 1e12
     sample = (f"each step: A[{rows},{K_DIM}] row panel of the 4096^3 GEMM @ B[{K_DIM},{N_DIM}] "
-              f"on {o.num_threads()} host threads (reference has no CPU path; oracle port)")
-    line = {"metric": "bf16_gemm_tflops_4096", "value": round(tflops, 5), "unit": "TFLOPS",
+              f"on {threads} host threads (the reference has no CPU path; oracle port)")
+    line = {"metric": METRIC, "value": round(tflops, 5), "unit": "TFLOPS",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "bf16 gemm M=N=K=4096, A[M,K] x B[K,N] row-major, U(-1,1), fp32 accumulate",
-                       "M": M_PER_RANK, "N": N_DIM, "K": K_DIM, "b_layout": "kn"},
+            "config": _config(args.layout, world),
             "impl": "reference",
-            "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOPS", "cores": o.num_threads(),
+            "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOPS", "cores": threads,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(tflops, 5), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -251,7 +274,8 @@ def sweep_configs():
     return out
 
 
-def time_config(M, N, K, layout, dist_kind, b200_gemm, target_ms=250.0, warmup=10, with_cublas=True, use_graph=True):
+def time_config(M, N, K, layout, dist_kind, b200_gemm, target_ms=250.0, warmup=10, with_cublas=True, use_graph=True,
+                with_split=True):
     """Device-time one GEMM shape back to back over rotating buffer sets larger than L2."""
     import math
     import torch
@@ -281,7 +305,7 @@ def time_config(M, N, K, layout, dist_kind, b200_gemm, target_ms=250.0, warmup=1
 
     res = {}
     variants = [("b200", ours), ("cublas", cublas)]
-    if b200_gemm.ops.workspace_bytes(M, N, K, layout) > 0:
+    if with_split and b200_gemm.ops.workspace_bytes(M, N, K, layout) > 0:
         variants.insert(1, ("b200_split_k", ours_splitk))
     for name, fn in variants:
         if name == "cublas" and not with_cublas:
@@ -673,11 +697,33 @@ def run_shape(args) -> int:
     return 0
 
 
+def _config(layout, world):
+    return {"workload": "bf16 gemm M=N=K=4096 per GPU, A[M,K] x B[K,N] row-major, U(-1,1), fp32 accumulate, "
+                        "bf16 out; N>1: one 4096-row A panel per rank, B broadcast from rank 0 over NCCL every "
+                        "step, C sharded",
+            "M_per_gpu": M_PER_RANK, "N": N_DIM, "K": K_DIM, "b_layout": layout,
+            "parallelism": f"row-sharded x{world}" if world > 1 else "single",
+            "l2": f"inputs larger than L2: rotating {ROTATE} A/B/C sets ({ROTATE * 96} MiB > 126 MB L2)"}
+
+
+def _step_fn(b200_gemm, A, B, C, layout, world):
+    """One step of the headline job: at N>1 rank 0's B is broadcast (NCCL) to
+    every rank, then every rank multiplies its A panel by it."""
+    import torch.distributed as dist
+
+    def step(i):
+        j = i % ROTATE
+        if world > 1:
+            dist.broadcast(B[j], src=0)
+        b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
+    return step
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layout", default="kn", choices=["kn", "nk"])
     ap.add_argument("--e2e-steps", type=int, default=30)
@@ -687,6 +733,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-rows", type=int, default=256)
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-config lines (BASELINE configs 2-4 at N=1, the row-sharded job at every N)")
     ap.add_argument("--sweep", action="store_true", help="time every single-GPU BASELINE config (one line each)")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="sweep: time direct launches instead of graph replay")
@@ -741,41 +789,59 @@ def main(argv=None) -> int:
     else:
         B = [torch.empty(b_shape, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
     C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+    stream = torch.cuda.current_stream(dev)
 
-    # B is broadcast once from rank 0 over NCCL (the BASELINE's row-sharded job).
+    # The first collective on a new communicator sets up its connections:
+    # warm it outside any timed region, then time the broadcast on its own.
     bcast_ms = None
     if world > 1:
+        for t in B:
+            dist.broadcast(t, src=0)
         torch.cuda.synchronize()
         _barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for t in B:
-            dist.broadcast(t, src=0)
-        e1.record()
+        reps = 5
+        e0.record(stream)
+        for r in range(reps):
+            for t in B:
+                dist.broadcast(t, src=0)
+        e1.record(stream)
         torch.cuda.synchronize()
-        bcast_ms = _max_over_ranks(e0.elapsed_time(e1) / ROTATE, world)
+        bcast_ms = _max_over_ranks(e0.elapsed_time(e1) / (reps * ROTATE), world)
 
-    stream = torch.cuda.current_stream(dev)
+    step = _step_fn(b200_gemm, A, B, C, layout, world)
     for i in range(args.warmup):
-        b200_gemm.gemm(A[i % ROTATE], B[i % ROTATE], b_layout=layout, out=C[i % ROTATE])
+        step(i)
     torch.cuda.synchronize()
     b200_gemm.check_status()
 
     props = torch.cuda.get_device_properties(dev)
     sampler = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # At N=1 a step is exactly one GEMM launch, and consecutive launches
+    # overlap through programmatic dependent launch: nothing else is put on
+    # the stream between them (an event record there would serialise them),
+    # so the mean launch duration is the timed region / steps.  At N>1 the
+    # broadcast sits between the GEMMs anyway; there each GEMM is bracketed
+    # by its own events.
+    per_launch = world > 1
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if per_launch else []
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if per_launch else []
 
     _barrier(world)
     torch.cuda.synchronize()
     sampler.start()
     t_beg.record(stream)
-    for i in range(args.steps):
-        j = i % ROTATE
-        starts[i].record(stream)
-        b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
-        ends[i].record(stream)
+    if per_launch:
+        for i in range(args.steps):
+            j = i % ROTATE
+            dist.broadcast(B[j], src=0)
+            starts[i].record(stream)
+            b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
+            ends[i].record(stream)
+    else:
+        for i in range(args.steps):
+            step(i)
     t_end.record(stream)
     torch.cuda.synchronize()
     _barrier(world)
@@ -783,12 +849,15 @@ def main(argv=None) -> int:
     b200_gemm.check_status()
 
     total_ms = _max_over_ranks(t_beg.elapsed_time(t_end), world)
-    launch_ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if per_launch:
+        launch_ms = statistics.fmean(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    else:
+        launch_ms = t_beg.elapsed_time(t_end) / args.steps
     launch_ms_max = _max_over_ranks(launch_ms, world)
     tflops = world * FLOPS_PER_STEP * args.steps / (total_ms / 1e3) / 1e12
     kernel_tflops = FLOPS_PER_STEP / (launch_ms_max / 1e3) / 1e12
 
-    # cuBLAS on the same GPU, same rotation (context only; not the product).
+    # cuBLAS on the same GPU, same rotation and loop shape (context only; not the product).
     cub_tflops = None
     if rank == 0 and args.cublas_steps != 0:
         n_cub = args.steps if args.cublas_steps < 0 else args.cublas_steps
@@ -804,15 +873,23 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         cub_tflops = FLOPS_PER_STEP * n_cub / (c0.elapsed_time(c1) / 1e3) / 1e12
 
+    # ---- N>1: parity of the sharded result and of the fused all-gather -------
+    parity = _multi_gpu_parity(A[0], B[0], layout, world, rank, b200_gemm) if world > 1 else None
+    del A, B, C
+    torch.cuda.empty_cache()
+
     # ---- end to end through the public API with host buffers ----------------
     e2e = _e2e(args, world, rank, dev, layout, b200_gemm)
+
+    # ---- BASELINE config 5 (row-sharded 131072x8192x8192) at this N ---------
+    rowshard = None if args.no_configs else _rowshard_object(args, world, rank, dev, b200_gemm)
 
     peaks = _peaks()
     long_region = total_ms >= 500.0
     peak = peaks["sustained"] if long_region else peaks["burst"]
     traffic = _traffic()
     line = {
-        "metric": "bf16_gemm_tflops_4096",
+        "metric": METRIC,
         "value": round(tflops, 2),
         "unit": "TFLOPS",
         "n_gpus": world,
@@ -824,24 +901,28 @@ def main(argv=None) -> int:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": "bf16 gemm M=N=K=4096 per GPU, A[M,K] x B[K,N] row-major, U(-1,1), fp32 accumulate, "
-                               "bf16 out; N>1: A row panels per rank, B broadcast once (NCCL), C sharded",
-                   "M_per_gpu": M, "N": N, "K": K, "b_layout": layout,
-                   "parallelism": f"row-sharded x{world}" if world > 1 else "single",
-                   "l2": f"rotating {ROTATE} input/output sets ({ROTATE * 96} MiB > 126 MB L2)"},
+        "config": _config(layout, world),
         "pct_of_peak": round(100.0 * tflops / world / peak, 2),
         "roofline": {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(kernel_tflops / peak, 4),
                      "peak_kind": ("sustained" if long_region else "burst") + f" bf16 cuBLAS, {peaks['source']}",
                      "traffic": (traffic or {}).get("bytes_per_launch"),
                      "algorithmic_flops_per_launch": FLOPS_PER_STEP,
-                     "avg_launch_ms": round(launch_ms_max, 5)},
+                     "avg_launch_ms": round(launch_ms_max, 5),
+                     "launch_timing": ("events around each GEMM launch (max over ranks)" if per_launch else
+                                       "timed region / steps: one GEMM launch per step, back to back")},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps,
         "e2e": e2e,
         "cublas_same_loop_tflops": round(cub_tflops, 2) if cub_tflops else None,
         "b_broadcast_ms": round(bcast_ms, 4) if bcast_ms is not None else None,
     }
+    if parity is not None:
+        line["parity"] = parity
+    if rowshard is not None:
+        line["rowshard"] = rowshard
+    if rank == 0 and world == 1 and not args.no_configs:
+        line["configs"] = _config_lines(b200_gemm, peaks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if rank == 0:
@@ -852,20 +933,174 @@ def main(argv=None) -> int:
     return 0
 
 
+def _multi_gpu_parity(a, b, layout, world, rank, b200_gemm):
+    """After the timed region at N>1: (1) the row-sharded C of every rank on
+    sampled rows against an fp32 CPU product of the same bf16 inputs (the
+    north_star bound: |dC| <= 2 bf16 ulp, relative Frobenius <= 1e-3);
+    (2) the GEMM with the C all-gather fused in (b200_gemm_bf16_allgather)
+    against the plain GEMM followed by NCCL's all-gather, bit for bit on every
+    rank.  Both flags are ANDed over the ranks."""
+    import torch
+    import torch.distributed as dist
+    from b200_gemm.dist import GatheredC, row_sharded_gemm_gather
+    M_loc, K = a.shape
+    N = b.shape[1] if layout == "kn" else b.shape[0]
+    M = M_loc * world
+    c = b200_gemm.gemm(a, b, b_layout=layout)
+    full = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    dist.all_gather_into_tensor(full, c)
+    # (1) sampled rows of this rank's panel
+    rows = torch.arange(0, M_loc, M_loc // 16, device=a.device)
+    a32 = a[rows].float().cpu()
+    b32 = (b if layout == "kn" else b.t()).float().cpu()
+    ref = a32 @ b32
+    got = c[rows].float().cpu()
+    rms = float(ref.pow(2).mean().sqrt())
+    mag = torch.clamp(ref.abs(), min=rms * 2.0 ** -8)
+    ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)
+    ok_elem = bool(((got - ref).abs() <= 2 * ulp).all())
+    frob = float((got - ref).norm() / max(float(ref.norm()), 1e-30))
+    ok1 = ok_elem and frob <= 1e-3
+    # (2) fused all-gather
+    gbuf = GatheredC(M, N)
+    fused = row_sharded_gemm_gather(a, b, gathered=gbuf, M=M, b_layout=layout, broadcast=False)
+    torch.cuda.synchronize()
+    ok2 = bool(torch.equal(fused, full))
+    b200_gemm.check_status()
+    gbuf.close()
+    flags = torch.tensor([int(ok1), int(ok2)], dtype=torch.int32, device=a.device)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    return {"rowshard": bool(flags[0]), "gather": bool(flags[1]), "rowshard_rel_frob": round(frob, 7),
+            "checked": f"rowshard: {len(rows)} rows per rank vs fp32 CPU product; gather: all {M}x{N} of C on "
+                       f"every rank vs GEMM + NCCL all_gather_into_tensor, bitwise"}
+
+
+def _rowshard_object(args, world, rank, dev, b200_gemm):
+    """BASELINE config 5 at this N: C = A B with A [131072, 8192] split into one
+    row panel per rank, B [8192, 8192] broadcast from rank 0, C sharded.
+    gemm_only_ms: the panel GEMMs alone; broadcast_plus_gemm_ms: B broadcast
+    (NCCL) then the GEMM, per step; both device-timed, max over ranks.  At N>1
+    rank 0 also runs the whole job alone (the N=1 figure in the same run), so
+    the speed-up is measured, not assumed."""
+    import torch
+    import torch.distributed as dist
+    from b200_gemm.dist import row_sharded_gemm, shard_rows
+    Mt, N, K = args.rowshard_m, 8192, 8192
+    flops = 2.0 * Mt * N * K
+    s, e = shard_rows(Mt, world, rank)
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    a = (torch.rand((e - s, K), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    b = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    c = torch.empty((e - s, N), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, budget_ms=300.0):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        fn()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        one = max(_max_over_ranks(e0.elapsed_time(e1), world), 1e-3)  # same step count on every rank
+        n = max(3, int(budget_ms / one))
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        return _max_over_ranks(e0.elapsed_time(e1) / n, world), n
+
+    gemm_ms, n1 = timed(lambda: row_sharded_gemm(a, b, M=Mt, b_layout="kn", out=c, broadcast=False))
+    both_ms, n2 = timed(lambda: row_sharded_gemm(a, b, M=Mt, b_layout="kn", out=c, broadcast=world > 1))
+    b200_gemm.check_status()
+    del a, c
+    out = {"workload": f"BASELINE config 5: A[{Mt},{K}] row panels x B[{K},{N}] (row-major), U(-1,1), "
+                       f"B broadcast from rank 0 (NCCL), C sharded; strong scaling",
+           "M": Mt, "N": N, "K": K, "panel_rows": e - s, "steps": [n1, n2],
+           "gemm_only_ms": round(gemm_ms, 4), "broadcast_plus_gemm_ms": round(both_ms, 4),
+           "gemm_only_tflops": round(flops / gemm_ms / 1e9, 1),
+           "tflops": round(flops / both_ms / 1e9, 1), "timing": "device, max over ranks"}
+    if world > 1:
+        # The whole job on rank 0 alone, in the same run, for the speed-up.
+        t1 = torch.zeros(1, dtype=torch.float64, device=dev)
+        if rank == 0:
+            ga = torch.Generator(device=dev).manual_seed(78)
+            a1 = (torch.rand((Mt, K), generator=ga, device=dev) * 2 - 1).to(torch.bfloat16)
+            c1 = torch.empty((Mt, N), dtype=torch.bfloat16, device=dev)
+            for _ in range(2):
+                b200_gemm.gemm(a1, b, b_layout="kn", out=c1)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 10
+            e0.record(stream)
+            for _ in range(reps):
+                b200_gemm.gemm(a1, b, b_layout="kn", out=c1)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t1[0] = e0.elapsed_time(e1) / reps
+            del a1, c1
+        dist.broadcast(t1, src=0)
+        one_gpu_ms = float(t1[0])
+        out["one_gpu_ms"] = round(one_gpu_ms, 4)
+        out["speedup_vs_one_gpu"] = round(one_gpu_ms / both_ms, 3)
+        out["speedup_gemm_only"] = round(one_gpu_ms / gemm_ms, 3)
+    del b
+    torch.cuda.empty_cache()
+    return out
+
+
+def _config_lines(b200_gemm, peaks):
+    """BASELINE configs 2-4 on this GPU (square sweep, skinny M <= 128, projection
+    shapes with ragged M), B [K,N]: ours and cuBLAS in the same loop, inputs
+    rotating over sets larger than L2, graph replay for GEMMs under 1 ms."""
+    out = []
+    for family, M, N, K, dist_kind in sweep_configs():
+        if family == "square" and M == 4096:
+            continue  # the headline above
+        t = time_config(M, N, K, "kn", dist_kind, b200_gemm, target_ms=60.0, warmup=5, with_split=False)
+        flops = 2.0 * M * N * K
+        nbytes = 2.0 * (M * K + K * N + M * N)
+        tf = flops / (t["b200"] / 1e3) / 1e12
+        gbs = nbytes / (t["b200"] / 1e3) / 1e9
+        hbm = family == "skinny"
+        out.append({"family": family, "M": M, "N": N, "K": K, "us": round(t["b200"] * 1e3, 2),
+                    "tflops": round(tf, 1), "gbs": round(gbs, 1), "bound": "hbm" if hbm else "tensor",
+                    "frac": round(gbs / peaks["hbm_gbs"] if hbm else tf / peaks["burst"], 4),
+                    "cublas_us": round(t["cublas"] * 1e3, 2) if "cublas" in t else None,
+                    "vs_cublas": round(t["cublas"] / t["b200"], 3) if "cublas" in t else None})
+    return out
+
+
 def _e2e(args, world, rank, dev, layout, b200_gemm):
     """Host buffers -> device -> GEMM -> host, every step, through the public API.
 
     Pipelined like a serving loop: three streams (copy in, compute, copy out)
     and two device buffer sets, so step i+1's host->device copy and step i-1's
     device->host copy overlap step i's GEMM.  Every step still moves its own
-    inputs in and its result out inside the timed region."""
+    inputs in and its result out inside the timed region.  At N>1 each rank
+    uploads its own A panel and a 1/N slice of B (rows of the [K,N] B) from its
+    pinned host memory, and the slices are all-gathered over NVLink (NCCL), so
+    no single PCIe link carries all of B."""
     import torch
     import torch.distributed as dist
     M, N, K = M_PER_RANK, N_DIM, K_DIM
     b_shape = (K, N) if layout == "kn" else (N, K)
-    g = torch.Generator().manual_seed(99 + rank)
+    rows_b = b_shape[0]
+    if world > 1 and rows_b % world != 0:
+        raise ValueError("B's rows must split evenly over the ranks")
+    slice_rows = rows_b // world
+    g = torch.Generator().manual_seed(99)
+    b_full = (torch.rand(b_shape, generator=g) * 2 - 1).to(torch.bfloat16)
+    b_h = b_full[rank * slice_rows:(rank + 1) * slice_rows].clone().pin_memory()
+    del b_full
+    g = torch.Generator().manual_seed(100 + rank)
     a_h = ((torch.rand((M, K), generator=g) * 2 - 1).to(torch.bfloat16)).pin_memory()
-    b_h = ((torch.rand(b_shape, generator=g) * 2 - 1).to(torch.bfloat16)).pin_memory() if rank == 0 else None
     c_h = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     a_d = [torch.empty((M, K), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     b_d = [torch.empty(b_shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
@@ -881,10 +1116,10 @@ def _e2e(args, world, rank, dev, layout, b200_gemm):
         j = i % 2
         with torch.cuda.stream(s_in):
             s_in.wait_event(ev_comp[j])  # the GEMM that last read a_d[j]/b_d[j] is done
-            if rank == 0:
-                b_d[j].copy_(b_h, non_blocking=True)
+            mine = b_d[j][rank * slice_rows:(rank + 1) * slice_rows]
+            mine.copy_(b_h, non_blocking=True)
             if world > 1:
-                dist.broadcast(b_d[j], src=0)
+                dist.all_gather_into_tensor(b_d[j], mine)
             a_d[j].copy_(a_h, non_blocking=True)
             ev_in[j].record(s_in)
         with torch.cuda.stream(s_comp):
@@ -915,13 +1150,15 @@ def _e2e(args, world, rank, dev, layout, b200_gemm):
     _barrier(world)
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
     tflops = world * FLOPS_PER_STEP * args.e2e_steps / (ms / 1e3) / 1e12
-    h2d = a_h.numel() * 2 + (b_h.numel() * 2 if rank == 0 else 0)
+    h2d = a_h.numel() * 2 + b_h.numel() * 2
     return {"value": round(tflops, 3), "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": c_h[0].numel() * 2, "steps": args.e2e_steps,
+            "d2h_bytes_per_step": c_h[0].numel() * 2, "bytes_per_step_are": "per rank",
+            "h2d_bytes_per_step_all_ranks": h2d * world, "steps": args.e2e_steps,
             "ms_per_step": round(ms / args.e2e_steps, 4),
-            "path": "pinned host A,B -> H2D -> b200_gemm.gemm (C ABI) -> D2H C every step; copy-in, GEMM and "
-                    "copy-out on three streams with two buffer sets (step i+1 in, i compute, i-1 out overlap)"
-                    + ("; B from rank 0 via NCCL broadcast" if world > 1 else "")}
+            "path": "pinned host A panel (+ this rank's 1/N slice of B) -> H2D"
+                    + (" -> NCCL all-gather of B" if world > 1 else "")
+                    + " -> b200_gemm.gemm (C ABI) -> D2H C, every step; copy-in, GEMM and copy-out on three "
+                      "streams with two buffer sets (step i+1 in, i compute, i-1 out overlap)"}
 
 
 if __name__ == "__main__":

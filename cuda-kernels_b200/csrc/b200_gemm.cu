@@ -423,10 +423,12 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   if (rc != B200_OK) return rc;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
 
-  if (K == 0) {  // empty reduction: C = 0
+  if (K == 0) {  // empty reduction: C = 0, in D's element type (bf16, or fp32 through the fused epilogue)
     if (epi.active) return B200_ERR_INVALID_ARG;  // bias / beta * C_in need K >= 1 (no kernel for K = 0)
-    return cudaMemset2DAsync(C, (size_t)ldc * 2, 0, (size_t)N * 2, (size_t)M, stream) == cudaSuccess ? B200_OK
-                                                                                                      : B200_ERR_CUDA;
+    const size_t esize = f32 ? 4 : 2;
+    return cudaMemset2DAsync(C, (size_t)ldc * esize, 0, (size_t)N * esize, (size_t)M, stream) == cudaSuccess
+               ? B200_OK
+               : B200_ERR_CUDA;
   }
   if (A == nullptr || B == nullptr) return B200_ERR_INVALID_ARG;
   if (lda < K) return B200_ERR_INVALID_ARG;
@@ -890,6 +892,22 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
                                                                                                       : B200_ERR_CUDA;
 }
 
+namespace {
+// The split-K plan gemm_impl would use for this shape when given a large
+// enough workspace: the same kernel choice (forced kernel, small-tile path,
+// M <= 128) and the same plan.  parts < 2: no split, no scratch.
+SplitPlan planned_split(const DeviceState& st, int64_t M, int64_t N, int64_t K) {
+  SplitPlan none{};
+  none.parts = 1;
+  if (M <= 0 || N <= 0 || K <= 0) return none;
+  const int force = g_force_kernel.load(std::memory_order_relaxed);
+  const bool pair = force == kForcePair || (force == kForceAuto && M > b200::kBM && !use_small_tiles(st, M, N));
+  if (!pair) return none;
+  const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
+  return plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st.max_pairs, kPairBN);
+}
+}  // namespace
+
 extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes) {
   if (bytes == nullptr || M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
   if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
@@ -897,11 +915,7 @@ extern "C" B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t 
   DeviceState* st = nullptr;
   const int rc = current_device_state(&st);
   if (rc != B200_OK) return rc;
-  const int force = g_force_kernel.load(std::memory_order_relaxed);
-  const bool pair = force == kForcePair || (force == kForceAuto && M > 128 && !use_small_tiles(*st, M, N));
-  if (!pair || M == 0 || N == 0 || K == 0) return B200_OK;
-  const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
-  const SplitPlan sp = plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st->max_pairs, kPairBN);
+  const SplitPlan sp = planned_split(*st, M, N, K);
   if (sp.parts >= 2) *bytes = sp.bytes();
   return B200_OK;
 }
@@ -999,11 +1013,38 @@ extern "C" B200_API const char* b200_gemm_version(void) { return "b200_gemm 0.1.
 // ---------------------------------------------------------------------------
 namespace {
 
-// Static split-K scratch: 16 MiB, enough for any shape on a 148-SM B200
-// (at most 15.75 MiB: 73 partial 256x256 fp32 tiles plus hand-off flags).
+// Static split-K scratch: 16 MiB, enough for any shape on a 148-SM B200.
+// There a launch holds at most 74 CTA pairs; a split plan over `rem` leftover
+// tiles in `parts` parts keeps rem x (parts - 1) x 2 partial tiles of
+// 128 x 256 fp32 (128 KiB each) plus one 8-byte flag per partial, and the
+// largest case, rem = 9 tiles in 8 parts, needs 126 partials = 15.75 MiB
+// plus 1 KiB of flags (the compile-time check below recomputes it).
 // Every GPU that loads this library holds it until the process exits.
 constexpr size_t kNoAllocScratchBytes = 16u << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Largest SplitPlan::bytes() plan_split can return for `pairs` CTA pairs and
+// 256-column tiles (every rem in [1, pairs), parts = min(pairs / rem, 8)).
+constexpr size_t max_split_bytes(int pairs) {
+  size_t best = 0;
+  for (int rem = 1; rem < pairs; ++rem) {
+    const int parts = pairs / rem < 8 ? pairs / rem : 8;
+    if (parts < 2) continue;
+    const size_t slots = (size_t)rem * (size_t)(parts - 1) * 2;
+    const size_t partial = (slots * (size_t)b200::kBM * (size_t)kPairBN * 4 + kWsAlign - 1) / kWsAlign * kWsAlign;
+    const size_t flags = (slots * 8 + kWsAlign - 1) / kWsAlign * kWsAlign;
+    if (partial + flags > best) best = partial + flags;
+  }
+  return best;
+}
+static_assert(max_split_bytes(74) <= kNoAllocScratchBytes,
+              "the static scratch must hold every split plan of a 148-SM B200 (74 CTA pairs)");
+
+// Scratch bytes the split plan of this shape needs (0 when it does not split).
+size_t sp_needs(const DeviceState& st, int64_t M, int64_t N, int64_t K) {
+  const SplitPlan sp = planned_split(st, M, N, K);
+  return sp.parts >= 2 ? sp.bytes() : 0;
+}
 
 struct NoAllocState {
   std::once_flag once;
@@ -1029,12 +1070,13 @@ extern "C" B200_API int b200_gemm_bf16_noalloc(const void* A, const void* B, voi
     na.rc = cudaGetSymbolAddress(&na.scratch, g_noalloc_scratch) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   });
   if (na.rc != B200_OK) return na.rc;
-  // Reject shapes whose split-K scratch would not fit the static buffer.
-  if (M > 0 && N > 0 && K > 0 && M > 128) {
-    const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
-    const SplitPlan sp = plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st->max_pairs, kPairBN);
-    if (sp.parts >= 2 && sp.bytes() > kNoAllocScratchBytes) return B200_ERR_SCRATCH_LIMIT;
-  }
+  // Reject shapes whose split-K scratch would not fit the static buffer
+  // (none on a 148-SM B200; a device with more co-resident CTA pairs could
+  // ask for more).  The plan is the one gemm_impl itself will choose, so the
+  // check follows the same kernel selection; an error is returned rather
+  // than a silent unsplit run, so a caller never gets a different summation
+  // order than b200_gemm_bf16_ws would give for the same shape.
+  if (sp_needs(*st, M, N, K) > kNoAllocScratchBytes) return B200_ERR_SCRATCH_LIMIT;
   // Nothing in the scratch needs clearing between calls: every partial tile is
   // written in full before it is read, and the hand-off flags are matched
   // against a tag that is new for every launch.

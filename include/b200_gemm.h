@@ -198,8 +198,9 @@ B200_API int b200_gemm_bf16_ex(const void* A, const void* B, void* D, int64_t M,
 
 /*
  * Workspace b200_gemm_bf16_ws wants for this shape on the current device
- * (0 when it would not split; at most ~19 MB on a B200).  Depends on the
- * device's SM count and on b200_gemm_set_kernel.
+ * (0 when it would not split; on a 148-SM B200 at most 15.75 MiB of fp32
+ * partial tiles plus 1 KiB of hand-off flags).  Depends on the device's SM
+ * count and on b200_gemm_set_kernel.
  */
 B200_API int b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int b_layout, size_t* bytes);
 

@@ -145,3 +145,31 @@ def test_epilogue_argument_errors():
     rc = lib.b200_gemm_bf16_ex(a.data_ptr(), b.data_ptr(), c.data_ptr(), 64, 64, 64, 64, 64, 64, 0, None, s)
     assert rc == _lib.B200_OK
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("ldd", [64, 72])
+def test_k_zero_fp32_d_is_zero_filled(ldd):
+    """K = 0 with fp32 D and no other epilogue term: D = 0 over its whole
+    [M, N] extent, with D's own 4-byte elements and row pitch (a bf16-sized
+    fill would clear half of each row and the wrong rows); the padding
+    columns beyond N keep their contents."""
+    M, N = 96, 60
+    import ctypes
+    from b200_gemm import _lib
+    lib = _lib.load()
+    a = torch.empty((M, 8), dtype=torch.bfloat16, device=DEV)
+    b = torch.empty((N, 8), dtype=torch.bfloat16, device=DEV)
+    buf = torch.full((M, ldd), 7.0, dtype=torch.float32, device=DEV)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    epi = _lib.Epilogue(alpha=1.0, beta=0.0, c_in=None, ldc_in=0, bias=None, d_dtype=_lib.B200_DTYPE_F32)
+    rc = lib.b200_gemm_bf16_ex(a.data_ptr(), b.data_ptr(), buf.data_ptr(), M, N, 0, 8, 8, ldd, 0,
+                               ctypes.byref(epi), s)
+    assert rc == _lib.B200_OK
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(buf[:, :N]) == 0
+    assert torch.all(buf[:, N:] == 7.0)
+    # the same through the Python API
+    out = torch.full((M, N), 5.0, dtype=torch.float32, device=DEV)
+    b200_gemm.gemm(a[:, :0], b[:, :0], out=out, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out) == 0

@@ -352,3 +352,49 @@ def test_split_k_workspace_arguments():
     torch.cuda.synchronize()
     assert torch.equal(c_small, c_ref)
     assert b200_gemm.ops.workspace_bytes(64, 4096, 4096, "nk") == 0  # skinny kernel: no split-K tail
+
+
+# BASELINE configs 2, 4 and 5 at their real sizes, where the dispatcher picks
+# other tiles than at 4096^3: 8192^3 and 16384^3 (square sweep), the
+# projection shapes with the widest N (128256: a ragged last 512-column tile,
+# over 2000 column blocks) and the ragged M = 8191 / 5000 on the 256 x 512
+# path, and the one-GPU panel of the row-sharded job (16384 x 8192 x 8192).
+# Inputs are generated on the GPU (seeded); every column of sampled rows
+# (first, last and random ones) is checked against the oracle with the bounds
+# of tests/_util.check_parity.
+LARGE_CONFIGS = [
+    (8192, 8192, 8192, "uniform"), (16384, 16384, 16384, "uniform"), (16384, 8192, 8192, "uniform"),
+    (8192, 128256, 4096, "normal"), (8191, 28672, 4096, "normal"), (8191, 4096, 14336, "normal"),
+    (5000, 128256, 4096, "normal"), (8191, 6144, 4096, "normal"),
+]
+
+
+def _dev_inputs(M, N, K, layout, dist, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    b_shape = (K, N) if layout == "kn" else (N, K)
+    if dist == "uniform":
+        a = (torch.rand((M, K), generator=g, device=DEV) * 2 - 1).to(torch.bfloat16)
+        b = (torch.rand(b_shape, generator=g, device=DEV) * 2 - 1).to(torch.bfloat16)
+    else:  # activations N(0, 1), weights N(0, 1/K)
+        a = torch.randn((M, K), generator=g, device=DEV).to(torch.bfloat16)
+        b = (torch.randn(b_shape, generator=g, device=DEV) * K ** -0.5).to(torch.bfloat16)
+    return a, b
+
+
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+@pytest.mark.parametrize("cfg", LARGE_CONFIGS, ids=lambda c: "x".join(map(str, c[:3])))
+def test_baseline_large_configs_sampled_rows(cfg, layout):
+    M, N, K, dist = cfg
+    a, b = _dev_inputs(M, N, K, layout, dist, seed=M + N + K)
+    c = b200_gemm.gemm(a, b, b_layout=layout)
+    torch.cuda.synchronize()
+    assert b200_gemm.check_status() == 0
+    rows = _rows(M, 24, M * 3 + K).to(DEV)
+    a_s = bits(a[rows])
+    b_bits = bits(b)
+    lay = 1 if layout == "kn" else 0
+    c_or = o.gemm_bf16(a_s, b_bits, lay)
+    c64, _ = o.gemm_f64(a_s, b_bits, lay)
+    check_parity(bits(c[rows]), c64, c_or, ctx=f"{M}x{N}x{K} {layout}")
+    del a, b, c
+    torch.cuda.empty_cache()
