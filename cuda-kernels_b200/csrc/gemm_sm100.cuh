@@ -173,6 +173,11 @@ struct GemmParams {
   uint64_t* flags;       // [split tiles][sk_parts-1][2 CTAs]
   EpilogueParams epi;
   int32_t num_out;       // output tensor maps each C tile is stored to (1, or one per rank when gathering)
+  // Balanced schedule (pair kernel, variable-width tiles; tile_schedule.h):
+  // units of 256 rows x 128 columns, units_per_row per row block, total_units
+  // in all, split into contiguous ranges over the launched CTA pairs.
+  int32_t vw_units_per_row;
+  int64_t vw_total_units;
 };
 
 // Output tensor maps of the gathering GEMM (b200_gemm_bf16_allgather): the
@@ -212,14 +217,20 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb,
 }
 
 struct WorkItem {
-  int mb, nb;    // tile coordinates
+  int mb, nb;    // tile coordinates (nb: column block of a fixed-width tile)
+  int col0;      // first column of the tile
+  int ncols;     // tile width in columns (BN for fixed-width tiles)
   int part;      // -1: whole K range; otherwise the split-K part index
   int kb0, kb1;  // K-block range [kb0, kb1)
   int split;     // index of the split tile (w.r.t. sk_first), or -1
 };
 
+// Work item w of the fixed-width schedule (tiles of BN columns, the split-K
+// tail after them); col0 / ncols are filled in by the caller, who knows BN.
 __device__ __forceinline__ WorkItem work_item(int w, const GemmParams& p) {
   WorkItem r;
+  r.col0 = 0;
+  r.ncols = 0;
   if (w < p.sk_first) {
     tile_coords(w, p, r.mb, r.nb);
     r.part = -1;
@@ -300,8 +311,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   // Launched with programmatic stream serialisation: the prologue above ran
   // while the previous kernel in the stream may still be finishing; wait for
-  // it before touching global memory, and let the next kernel start its own
-  // prologue as early as possible.
+  // it before loading anything, and let the next kernel start its own
+  // prologue as early as possible.  Before waiting, the producer asks L2 for
+  // the operand tiles of its first tile's first ring's worth of K-blocks (a
+  // prefetch only warms L2, the point of coherence, so it cannot expose data
+  // the previous kernel is still writing).
+  if (warp == 0 && lane == 0 && (int)blockIdx.x < p.num_tiles) {
+    int mb, nb;
+    tile_coords(blockIdx.x, p, mb, nb);
+    const int kb_end = min(p.num_k_blk, STAGES);
+    for (int kb = 0; kb < kb_end; ++kb) {
+      tma_prefetch_l2_2d(&tmA, kb * kBK, mb * kBM);
+      if constexpr (!B_MN) {
+        tma_prefetch_l2_2d(&tmB, kb * kBK, nb * BN);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, nb * BN + 64 * j, kb * kBK);
+      }
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();
 
