@@ -33,7 +33,6 @@ B200_KERNEL_AUTO = 0
 B200_KERNEL_SINGLE = 1
 B200_KERNEL_PAIR = 2
 B200_KERNEL_SKINNY = 3
-B200_KERNEL_PAIR_BALANCED = 4
 
 class Epilogue(ctypes.Structure):
     """struct b200_epilogue (include/b200_gemm.h)."""

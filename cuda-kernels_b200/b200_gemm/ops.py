@@ -257,11 +257,11 @@ def set_timeout_ns(ns: int, device: torch.device | int | None = None) -> None:
 
 
 _KERNELS = {"auto": _lib.B200_KERNEL_AUTO, "single": _lib.B200_KERNEL_SINGLE, "pair": _lib.B200_KERNEL_PAIR,
-            "skinny": _lib.B200_KERNEL_SKINNY, "pair_balanced": _lib.B200_KERNEL_PAIR_BALANCED}
+            "skinny": _lib.B200_KERNEL_SKINNY}
 
 
 def set_kernel(which: str) -> None:
-    """Force a kernel for later calls ("auto", "single", "pair", "skinny", "pair_balanced"); for tests and tuning."""
+    """Force a kernel for later calls ("auto", "single", "pair", "skinny"); for tests and tuning."""
     if which not in _KERNELS:
         raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
     rc = _lib.load().b200_gemm_set_kernel(_KERNELS[which])

@@ -66,7 +66,7 @@ struct SkinnyCfg<128> { static constexpr int kStages = 6; };
 constexpr int kMaxClusterSplits = 8;  // portable cluster size limit
 
 // Kernel selection override (b200_gemm_set_kernel): process-wide.
-enum ForceKernel { kForceAuto = 0, kForceSingle = 1, kForcePair = 2, kForceSkinny = 3, kForcePairBalanced = 4 };
+enum ForceKernel { kForceAuto = 0, kForceSingle = 1, kForcePair = 2, kForceSkinny = 3 };
 std::atomic<int> g_force_kernel{kForceAuto};
 
 struct DeviceState {
@@ -193,8 +193,6 @@ int init_device(int dev, DeviceState& st) {
       {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false>, wide_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, true>, wide_smem},
       {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, true>, wide_smem},
-      {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, false, true>, wide_smem},
-      {(const void*)b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false, true>, wide_smem},
       {(const void*)b200::gemm_bf16_pair_gather_kernel<false>, pair_smem},
       {(const void*)b200::gemm_bf16_pair_gather_kernel<true>, pair_smem},
   };
@@ -442,10 +440,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   // small to occupy the GPU with pairs (use_small_tiles).  (The single-CTA
   // 128 x 256 kernel remains for callers that force it with
   // b200_gemm_set_kernel.)
-  const int force_req = outs != nullptr ? kForcePair : g_force_kernel.load(std::memory_order_relaxed);
-  // The balanced schedule is a pair-kernel schedule: forcing it forces the pair kernel.
-  const bool force_balanced = force_req == kForcePairBalanced;
-  const int force = force_balanced ? kForcePair : force_req;
+  const int force = outs != nullptr ? kForcePair : g_force_kernel.load(std::memory_order_relaxed);
   if (force == kForceSkinny && M > 128) return B200_ERR_INVALID_ARG;
   if (force == kForceSkinny || (force == kForceAuto && M <= 128)) {
     if (M <= 16) return launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
@@ -484,30 +479,10 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   const bool use_wide = use_pair && !use_split && !fused_epi &&
                         m_blk_pair * ((N + kPairWideBN - 1) / kPairWideBN) >= max_pairs &&
                         wave_eff(kPairWideBN) >= 0.97 * wave_eff(kPairBN);
-  // Balanced schedule of variable-width tiles (tile_schedule.h) when the
-  // fixed tiling leaves much of its last wave idle: compare the work of the
-  // busiest pair, in units of 256 x 128, and take the balanced schedule when
-  // it is at least 8 % lighter (4096^3: 7 units against 8).  Each pair then
-  // sweeps its own row-block range, re-reading A and B from L2 for every
-  // tile, so only for operands that fit in L2 together (<= 96 MB).  Same
-  // product, same K order per tile: bit-identical to the fixed tiling.
-  bool use_vw = false;
-  int64_t vw_units_per_row = 0, vw_total = 0;
-  if (use_pair && !use_split && !fused_epi) {
-    vw_units_per_row = (N + b200::kUnitCols - 1) / b200::kUnitCols;
-    vw_total = m_blk_pair * vw_units_per_row;
-    const int64_t busiest_vw = (vw_total + max_pairs - 1) / max_pairs;
-    const int64_t fixed_bn = use_wide ? kPairWideBN : kPairBN;
-    const int64_t fixed_tiles = m_blk_pair * ((N + fixed_bn - 1) / fixed_bn);
-    const int64_t busiest_fixed = (fixed_tiles + max_pairs - 1) / max_pairs * (fixed_bn / b200::kUnitCols);
-    const double operand_bytes = 2.0 * ((double)M * (double)K + (double)K * (double)N);
-    use_vw = force_balanced ||
-             (force == kForceAuto && (double)busiest_vw * 1.08 <= (double)busiest_fixed && operand_bytes <= 96e6);
-  }
-  const uint32_t bn = use_small           ? (uint32_t)kSmallBN
-                      : !use_pair         ? (uint32_t)kBN
-                      : use_wide || use_vw ? (uint32_t)kPairWideBN
-                                          : (uint32_t)kPairBN;
+  const uint32_t bn = use_small   ? (uint32_t)kSmallBN
+                      : !use_pair ? (uint32_t)kBN
+                      : use_wide  ? (uint32_t)kPairWideBN
+                                  : (uint32_t)kPairBN;
   // B rows (K-major) one TMA box covers: a pair CTA loads 128-column blocks.
   const uint32_t b_rows = use_pair ? 128u : bn;
 
@@ -595,11 +570,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
       p.epoch = ((uint64_t)process_salt() << 32) | (uint64_t)n;
     }
   }
-  if (use_vw) {
-    p.vw_units_per_row = (int32_t)vw_units_per_row;
-    p.vw_total_units = vw_total;
-  }
-  const int64_t work = use_vw ? vw_total : (int64_t)p.num_work;
+  const int64_t work = p.num_work;
   const int pairs = (int)(work < max_pairs ? work : max_pairs);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -611,8 +582,8 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(b200::kNumThreads, 1, 1);
-  cfg.dynamicSmemBytes = (use_wide || use_vw) ? b200::PairSmemPlan<kPairWideBN, kPairWideStages>::kAllocBytes
-                                              : b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
+  cfg.dynamicSmemBytes = use_wide ? b200::PairSmemPlan<kPairWideBN, kPairWideStages>::kAllocBytes
+                                  : b200::PairSmemPlan<kPairBN, kPairStages>::kAllocBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
@@ -635,9 +606,7 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
                      : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_gather_kernel<false>, tmA, tmB, *outs, p);
     return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
-  static const PairKernel kPairVW[2] = {b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, false, false, true>,
-                                        b200::gemm_bf16_pair_kernel<kPairWideBN, kPairWideStages, true, false, true>};
-  const PairKernel kern = use_vw ? kPairVW[p.b_mn_major ? 1 : 0] : kPair[use_wide ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
+  const PairKernel kern = kPair[use_wide ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
@@ -932,8 +901,7 @@ SplitPlan planned_split(const DeviceState& st, int64_t M, int64_t N, int64_t K) 
   none.parts = 1;
   if (M <= 0 || N <= 0 || K <= 0) return none;
   const int force = g_force_kernel.load(std::memory_order_relaxed);
-  const bool pair = force == kForcePair || force == kForcePairBalanced ||
-                    (force == kForceAuto && M > b200::kBM && !use_small_tiles(st, M, N));
+  const bool pair = force == kForcePair || (force == kForceAuto && M > b200::kBM && !use_small_tiles(st, M, N));
   if (!pair) return none;
   const int64_t tiles = ((M + b200::kPairBM - 1) / b200::kPairBM) * ((N + kPairBN - 1) / kPairBN);
   return plan_split(tiles, (int32_t)((K + b200::kBK - 1) / b200::kBK), st.max_pairs, kPairBN);
@@ -1011,7 +979,7 @@ extern "C" B200_API int b200_gemm_selftest_wait_timeout(uint64_t timeout_ns, voi
 }
 
 extern "C" B200_API int b200_gemm_set_kernel(int which) {
-  if (which < kForceAuto || which > kForcePairBalanced) return B200_ERR_INVALID_ARG;
+  if (which < kForceAuto || which > kForceSkinny) return B200_ERR_INVALID_ARG;
   g_force_kernel.store(which, std::memory_order_relaxed);
   return B200_OK;
 }

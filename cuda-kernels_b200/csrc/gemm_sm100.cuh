@@ -173,11 +173,6 @@ struct GemmParams {
   uint64_t* flags;       // [split tiles][sk_parts-1][2 CTAs]
   EpilogueParams epi;
   int32_t num_out;       // output tensor maps each C tile is stored to (1, or one per rank when gathering)
-  // Balanced schedule (pair kernel, variable-width tiles; tile_schedule.h):
-  // units of 256 rows x 128 columns, units_per_row per row block, total_units
-  // in all, split into contiguous ranges over the launched CTA pairs.
-  int32_t vw_units_per_row;
-  int64_t vw_total_units;
 };
 
 // Output tensor maps of the gathering GEMM (b200_gemm_bf16_allgather): the
@@ -217,20 +212,14 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mb,
 }
 
 struct WorkItem {
-  int mb, nb;    // tile coordinates (nb: column block of a fixed-width tile)
-  int col0;      // first column of the tile
-  int ncols;     // tile width in columns (BN for fixed-width tiles)
+  int mb, nb;    // tile coordinates
   int part;      // -1: whole K range; otherwise the split-K part index
   int kb0, kb1;  // K-block range [kb0, kb1)
   int split;     // index of the split tile (w.r.t. sk_first), or -1
 };
 
-// Work item w of the fixed-width schedule (tiles of BN columns, the split-K
-// tail after them); col0 / ncols are filled in by the caller, who knows BN.
 __device__ __forceinline__ WorkItem work_item(int w, const GemmParams& p) {
   WorkItem r;
-  r.col0 = 0;
-  r.ncols = 0;
   if (w < p.sk_first) {
     tile_coords(w, p, r.mb, r.nb);
     r.part = -1;

@@ -30,7 +30,6 @@
 
 #include "gemm_sm100.cuh"
 #include "ptx_sm100.cuh"
-#include "tile_schedule.h"
 
 namespace b200 {
 
@@ -69,64 +68,15 @@ struct PairSmemPlan {
   static_assert(kAccN * BN <= kTmemCols, "accumulators must fit in TMEM");
 };
 
-// The tiles one CTA pair computes, in order.  Fixed-width schedule: work
-// items pair, pair + pairs, ... (whole BN-column tiles in grouped order, then
-// the split-K parts of the last wave's tiles).  Balanced schedule (VW): the
-// pair's contiguous range of 256 x 128 units, covered by tiles of 128 to 512
-// columns (tile_schedule.h).  The producer, the MMA issuer and the epilogue
-// each walk their own cursor over the same sequence.
-template <int BN, bool VW>
-struct TileCursor {
-  int64_t pos, end;
-  int step;
-  __device__ __forceinline__ TileCursor(const GemmParams& p, int pair, int num_pairs) {
-    if constexpr (VW) {
-      const BalancedSchedule s{p.vw_units_per_row, p.vw_total_units, num_pairs};
-      balanced_range(s, pair, pos, end);
-      step = 0;
-    } else {
-      pos = pair;
-      end = p.num_work;
-      step = num_pairs;
-    }
-  }
-  __device__ __forceinline__ bool next(const GemmParams& p, WorkItem& wk) {
-    if (pos >= end) return false;
-    if constexpr (VW) {
-      const BalancedSchedule s{p.vw_units_per_row, p.vw_total_units, (int32_t)(gridDim.x >> 1)};
-      const VarTile t = balanced_tile(s, pos, end);
-      wk.mb = t.mb;
-      wk.nb = -1;
-      wk.col0 = t.col0;
-      wk.ncols = t.units * kUnitCols;
-      wk.part = -1;
-      wk.kb0 = 0;
-      wk.kb1 = p.num_k_blk;
-      wk.split = -1;
-      pos += t.units;
-    } else {
-      wk = work_item((int)pos, p);
-      wk.col0 = wk.nb * BN;
-      wk.ncols = BN;
-      pos += step;
-    }
-    return true;
-  }
-};
-
 // Kernel body, shared by the plain/fused kernel (one output map) and the
 // gathering kernel (one output map per rank: every C tile is stored to each).
-// VW: balanced schedule of variable-width tiles (BN = 512 is then the widest
-// tile; a tile of w columns runs ceil(w / 256) pair MMAs per K slice, of
-// N = 256, or N = 128 for a trailing 128-column part).
-template <int BN, int STAGES, bool B_MN, bool EPI, bool VW = false>
+template <int BN, int STAGES, bool B_MN, bool EPI>
 __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
                                                const CUtensorMap* outs, const int n_out, const GemmParams& p) {
   using Plan = PairSmemPlan<BN, STAGES>;
   constexpr int kNSub = Plan::kNSub;
   constexpr int kAccN = Plan::kAccN;
   static_assert(BN == 256 || BN == 512, "pair tiles are 256 x 256 or 256 x 512");
-  static_assert(!VW || (BN == 512 && kAccN == 1 && !EPI), "variable-width tiles: plain epilogue, one 512-column accumulator");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -183,28 +133,21 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
   // this CTA's operand tiles of its first ring's worth of K-blocks (a
   // prefetch only warms L2, the point of coherence, so it cannot expose data
   // the previous kernel is still writing).
-  // Sub-tile h of a tile: pair MMA columns [col0 + 256 h, + wh), wh = 256
-  // (or 128 for the trailing part of a variable-width tile); CTA r holds B
-  // columns [col0 + 256 h + r wh / 2, + wh / 2).
-  auto sub_cols = [&](const WorkItem& wk, int h) { return VW ? min(Plan::kMmaN, wk.ncols - h * Plan::kMmaN) : Plan::kMmaN; };
-  auto num_sub = [&](const WorkItem& wk) { return VW ? (wk.ncols + Plan::kMmaN - 1) / Plan::kMmaN : kNSub; };
-  if (warp == 0 && lane == 0) {
-    TileCursor<BN, VW> cur(p, pair, num_pairs);
-    WorkItem wk;
-    if (cur.next(p, wk)) {
-      const int row0 = wk.mb * kPairBM + (int)rank * kBM;
-      const int kb_end = min(wk.kb1, wk.kb0 + STAGES);
-      const int nsub = num_sub(wk);
-      for (int kb = wk.kb0; kb < kb_end; ++kb) {
-        tma_prefetch_l2_2d(&tmA, kb * kBK, row0);
-        for (int h = 0; h < nsub; ++h) {
-          const int wh = sub_cols(wk, h);
-          const int colh = wk.col0 + h * Plan::kMmaN + (int)rank * (wh / 2);
-          if constexpr (!B_MN) {
-            tma_prefetch_l2_2d(&tmB, kb * kBK, colh);
-          } else {
-            for (int j = 0; j < wh / 128; ++j) tma_prefetch_l2_2d(&tmB, colh + 64 * j, kb * kBK);
-          }
+  if (warp == 0 && lane == 0 && pair < p.num_work) {
+    const WorkItem wk = work_item(pair, p);
+    const int row0 = wk.mb * kPairBM + (int)rank * kBM;
+    const int col0 = wk.nb * BN + (int)rank * Plan::kSubCols;
+    const int kb_end = min(wk.kb1, wk.kb0 + STAGES);
+    for (int kb = wk.kb0; kb < kb_end; ++kb) {
+      tma_prefetch_l2_2d(&tmA, kb * kBK, row0);
+#pragma unroll
+      for (int h = 0; h < kNSub; ++h) {
+        const int colh = col0 + h * Plan::kMmaN;
+        if constexpr (!B_MN) {
+          tma_prefetch_l2_2d(&tmB, kb * kBK, colh);
+        } else {
+#pragma unroll
+          for (int j = 0; j < Plan::kSubCols / 64; ++j) tma_prefetch_l2_2d(&tmB, colh + 64 * j, kb * kBK);
         }
       }
     }
@@ -223,34 +166,27 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
-      TileCursor<BN, VW> cur(p, pair, num_pairs);
-      WorkItem wk;
-      while (ok && cur.next(p, wk)) {
+      for (int w = pair; w < p.num_work && ok; w += num_pairs) {
+        const WorkItem wk = work_item(w, p);
         const int row0 = wk.mb * kPairBM + (int)rank * kBM;
-        const int nsub = num_sub(wk);
-        // Bytes both CTAs load per K-block (the leader's full barrier counts
-        // them all): A rows, and per sub-tile one 128-row box of K-major B,
-        // or wh / 128 boxes of 64 columns of MN-major B, per CTA.
-        uint32_t stage_tx = Plan::kABytes;
-        for (int h = 0; h < nsub; ++h) stage_tx += B_MN ? (uint32_t)(sub_cols(wk, h) / 128) * (64 * kBK * 2) : Plan::kBSubBytes;
-        stage_tx *= 2;
+        const int col0 = wk.nb * BN + (int)rank * Plan::kSubCols;  // + h * kMmaN for sub-tile h
         for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
             ok = false;
             break;
           }
           const uint32_t fb = mapa_shared(full_bar(stage), 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), stage_tx);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * Plan::kStageBytes);
           tma_load_2d_pair(sA + stage * Plan::kABytes, &tmA, fb, kb * kBK, row0, pol);
-          for (int h = 0; h < nsub; ++h) {
+#pragma unroll
+          for (int h = 0; h < kNSub; ++h) {
             const uint32_t dstB = sB + stage * Plan::kBBytes + h * Plan::kBSubBytes;
-            const int wh = sub_cols(wk, h);
-            const int colh = wk.col0 + h * Plan::kMmaN + (int)rank * (wh / 2);
+            const int colh = col0 + h * Plan::kMmaN;
             if constexpr (!B_MN) {
-              // one box of 128 rows; a 128-column sub-tile uses its first 64
               tma_load_2d_pair(dstB, &tmB, fb, kb * kBK, colh, pol);
             } else {
-              for (int j = 0; j < wh / 128; ++j) {
+#pragma unroll
+              for (int j = 0; j < Plan::kSubCols / 64; ++j) {
                 tma_load_2d_pair(dstB + j * (64 * kBK * 2), &tmB, fb, colh + 64 * j, kb * kBK, pol);
               }
             }
@@ -283,7 +219,6 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
     // ---- MMA issuer (leader CTA only) ---------------------------------------------
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(kPairBM, Plan::kMmaN, false, B_MN);
-      constexpr uint32_t idesc128 = idesc_bf16_f32(kPairBM, 128, false, B_MN);  // trailing 128-column part (VW)
       // Descriptors of stage 0; later stages and K slices only move the
       // start-address field (bits 0..13, address >> 4), which never carries.
       //   A, K-major SW128: 128-byte rows, 8-row groups 1024 B apart; the k-th
@@ -298,17 +233,10 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      // Variable-width tiles use the 256-column halves of the accumulator
-      // unevenly (a half is skipped by narrow tiles): one phase per half.
-      uint32_t half_phase[kNSub];
-#pragma unroll
-      for (int h = 0; h < kNSub; ++h) half_phase[h] = 0u;
       bool ok = true;
-      TileCursor<BN, VW> cur(p, pair, num_pairs);
-      WorkItem wk;
-      while (ok && cur.next(p, wk)) {
+      for (int w = pair; w < p.num_work && ok; w += num_pairs) {
+        const WorkItem wk = work_item(w, p);
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        const int nsub = num_sub(wk);
         // Sub-tile h of this accumulator may be written once the epilogue has
         // drained it (checked right before its first MMA of the tile).
         bool free_h[kNSub];
@@ -324,10 +252,8 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
           const uint64_t bd = b_desc0 + (uint64_t)((stage * Plan::kBBytes) >> 4);
 #pragma unroll
           for (int h = 0; h < kNSub; ++h) {
-            if (VW && h >= nsub) break;
             if (!free_h[h]) {
-              const uint32_t ph = VW ? half_phase[h] : acc_phase;
-              if (!mbar_wait(acce_bar(acc, h), ph ^ 1u, p.timeout_ns, abort_flag)) {
+              if (!mbar_wait(acce_bar(acc, h), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
                 ok = false;
                 break;
               }
@@ -335,10 +261,9 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
               free_h[h] = true;
             }
             const uint64_t bdh = bd + (uint64_t)((h * Plan::kBSubBytes) >> 4);
-            const uint32_t id = (VW && sub_cols(wk, h) == 128) ? idesc128 : idesc;
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
-              umma_bf16_pair(d_tmem + (uint32_t)(h * Plan::kMmaN), ad + 2u * k, bdh + kBStep * k, id,
+              umma_bf16_pair(d_tmem + (uint32_t)(h * Plan::kMmaN), ad + 2u * k, bdh + kBStep * k, idesc,
                              (kb != wk.kb0 || k != 0) ? 1u : 0u);
             }
           }
@@ -352,12 +277,6 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
         }
         if (!ok) break;
         umma_commit_pair_both(accf_bar(acc));  // accumulator ready for both CTAs' epilogues
-        if constexpr (VW) {
-#pragma unroll
-          for (int h = 0; h < kNSub; ++h) {
-            if (h < nsub) half_phase[h] ^= 1u;
-          }
-        }
         if (++acc == kAccN) {
           acc = 0;
           acc_phase ^= 1u;
@@ -376,13 +295,12 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
-    TileCursor<BN, VW> cur(p, pair, num_pairs);
-    WorkItem wk;
-    while (cur.next(p, wk)) {
+    for (int w = pair; w < p.num_work; w += num_pairs) {
+      const WorkItem wk = work_item(w, p);
       if constexpr (EPI) {
         if (wk.part < 0 || wk.part == p.sk_parts - 1) {
           epilogue_prefetch_row(p.epi, wk.mb * kPairBM + (int)rank * kBM + q * kEpiRowsPerWarp + (int)lane,
-                                wk.col0, wk.ncols, p.M, p.N);
+                                wk.nb * BN, BN, p.M, p.N);
         }
       }
       const bool got = mbar_wait(accf_bar(acc), acc_phase, p.timeout_ns, abort_flag);
@@ -412,15 +330,14 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
         }
         named_bar_sync(1, kEpiWarps * 32);
       }
-      const int nchunks = wk.ncols / kEpiCols;
 #pragma unroll 1
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = 0; c < BN / kEpiCols; ++c) {
         uint32_t r0[32], r1[32];
         tmem_ld_32x32b_x32(t_row + c * kEpiCols, r0);
         tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, r1);
         tmem_ld_wait_regs(r0);
         tmem_ld_wait_regs(r1);
-        if (((c + 1) * kEpiCols) % Plan::kMmaN == 0 || c + 1 == nchunks) {
+        if (((c + 1) * kEpiCols) % Plan::kMmaN == 0) {
           // Sub-tile (c * 64) / 256 of this accumulator is drained: hand it back.
           tc_fence_before();
           __syncwarp();
@@ -453,7 +370,7 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
             }
           }
         }
-        const int n0 = wk.col0 + c * kEpiCols;
+        const int n0 = wk.nb * BN + c * kEpiCols;
         if constexpr (EPI) {
           if (p.epi.active) {
             epilogue_row32(r0, p.epi, row + (int)lane, n0, p.M, p.N);
@@ -517,14 +434,14 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
   }
 }
 
-template <int BN, int STAGES, bool B_MN, bool EPI = false, bool VW = false>
+template <int BN, int STAGES, bool B_MN, bool EPI = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const __grid_constant__ GemmParams p) {
 #if B200_NO_SM100A_FEATURES
   if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
 #else
-  pair_gemm_body<BN, STAGES, B_MN, EPI, VW>(tmA, tmB, &tmC, 1, p);
+  pair_gemm_body<BN, STAGES, B_MN, EPI>(tmA, tmB, &tmC, 1, p);
 #endif
 }
 

@@ -249,11 +249,6 @@ B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns);
  *   B200_KERNEL_SINGLE (1) one CTA per 128 x 256 tile, any M
  *   B200_KERNEL_PAIR   (2) CTA pair per 256 x 256 tile, any M
  *   B200_KERNEL_SKINNY (3) swap-AB split-K, M <= 128 only (else B200_ERR_INVALID_ARG at launch)
- *   B200_KERNEL_PAIR_BALANCED (4) CTA pairs on the balanced schedule of
- *                          128..512-column tiles (every pair gets an equal
- *                          share of 256 x 128 units; chosen automatically
- *                          when the fixed tiles would leave much of the last
- *                          wave idle, e.g. 4096^3), any M
  * For testing and tuning; every choice computes the same product.  No
  * reference counterpart (the reference picks a kernel by calling a different
  * launcher, bf16_matmul/matmul.cpp:44-56).
@@ -262,7 +257,6 @@ B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns);
 #define B200_KERNEL_SINGLE 1
 #define B200_KERNEL_PAIR 2
 #define B200_KERNEL_SKINNY 3
-#define B200_KERNEL_PAIR_BALANCED 4
 B200_API int b200_gemm_set_kernel(int which);
 
 /*

