@@ -959,7 +959,10 @@ def _multi_gpu_parity(a, b, layout, world, rank, b200_gemm):
     mag = torch.clamp(ref.abs(), min=rms * 2.0 ** -8)
     ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)
     ok_elem = bool(((got - ref).abs() <= 2 * ulp).all())
-    frob = float((got - ref).norm() / max(float(ref.norm()), 1e-30))
+    # Rounding the exact product to bf16 alone costs ~1.6e-3 relative
+    # Frobenius error, so the 1e-3 bound compares two bf16-rounded results.
+    ref16 = ref.bfloat16().float()
+    frob = float((got - ref16).norm() / max(float(ref.norm()), 1e-30))
     ok1 = ok_elem and frob <= 1e-3
     # (2) fused all-gather
     gbuf = GatheredC(M, N)
@@ -971,7 +974,8 @@ def _multi_gpu_parity(a, b, layout, world, rank, b200_gemm):
     flags = torch.tensor([int(ok1), int(ok2)], dtype=torch.int32, device=a.device)
     dist.all_reduce(flags, op=dist.ReduceOp.MIN)
     return {"rowshard": bool(flags[0]), "gather": bool(flags[1]), "rowshard_rel_frob": round(frob, 7),
-            "checked": f"rowshard: {len(rows)} rows per rank vs fp32 CPU product; gather: all {M}x{N} of C on "
+            "checked": f"rowshard: {len(rows)} rows per rank vs fp32 CPU product (|dC| <= 2 bf16 ulp; relative "
+                       f"Frobenius vs the product rounded to bf16 <= 1e-3); gather: all {M}x{N} of C on "
                        f"every rank vs GEMM + NCCL all_gather_into_tensor, bitwise"}
 
 

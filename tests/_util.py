@@ -73,3 +73,25 @@ def check_parity(c_bits: np.ndarray, c_true: np.ndarray, c_oracle_bits: np.ndarr
     assert max_ulp <= max_ulp_vs_oracle + 1e-9, f"{ctx}: {max_ulp:.2f} bf16 ulp from the oracle"
     assert frac < 0.01, f"{ctx}: {frac:.3%} of elements differ from the oracle"
     return {"max_err_over_tol": worst, "rel_frob": frob, "max_ulp_vs_oracle": max_ulp, "frac_diff": frac}
+
+
+def free_port() -> int:
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def spawn_ranks(fn, make_args, nprocs: int):
+    """torch.multiprocessing.spawn of `nprocs` ranks with a fresh rendezvous
+    port (make_args(port) builds the argument tuple).  A port can be taken by
+    another process between choosing and binding it; that case (EADDRINUSE)
+    is retried with a new port, any other failure is raised."""
+    import torch.multiprocessing as mp
+    for attempt in range(4):
+        try:
+            return mp.spawn(fn, args=make_args(free_port()), nprocs=nprocs, join=True)
+        except mp.ProcessRaisedException as e:
+            if "EADDRINUSE" in str(e) and attempt < 3:
+                continue
+            raise

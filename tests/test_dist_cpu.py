@@ -12,6 +12,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from tests._util import spawn_ranks
+
 from b200_gemm.dist import chunk_bounds, gather_rows, row_sharded_gemm, shard_rows
 
 
@@ -75,7 +77,7 @@ def _worker(rank, world, port, M, N, K, layout, chunks, result_dir):
 def test_row_sharded_gemm_two_ranks(tmp_path, layout, chunks):
     M, N, K = 37, 200, 72  # ragged panels (19 + 18 rows), N not a multiple of the chunk
     world = 2
-    mp.spawn(_worker, args=(world, _free_port(), M, N, K, layout, chunks, str(tmp_path)), nprocs=world, join=True)
+    spawn_ranks(_worker, lambda port: (world, port, M, N, K, layout, chunks, str(tmp_path)), world)
     c = torch.load(os.path.join(tmp_path, "c.pt"))
     from oracle import oracle as o
     from tests._util import bits, uniform_bf16

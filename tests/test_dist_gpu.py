@@ -9,6 +9,8 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from tests._util import spawn_ranks
+
 pytestmark = pytest.mark.gpu
 
 
@@ -52,7 +54,7 @@ def test_row_sharded_gemm_nccl(tmp_path, layout, chunks):
         pytest.skip("needs at least 2 GPUs")
     world = min(world, 8)
     M, N, K = 4099, 1000, 520  # ragged panels and a ragged last chunk
-    mp.spawn(_worker, args=(world, _free_port(), M, N, K, layout, chunks, str(tmp_path)), nprocs=world, join=True)
+    spawn_ranks(_worker, lambda port: (world, port, M, N, K, layout, chunks, str(tmp_path)), world)
     c = torch.load(os.path.join(tmp_path, "c.pt"))
     from oracle import oracle as o
     from tests._util import bits, check_parity, uniform_bf16
@@ -103,8 +105,7 @@ def test_gemm_with_fused_allgather(tmp_path, layout):
         pytest.skip("needs at least 2 GPUs")
     world = min(world, 8)
     M, N, K, steps = 2051, 1000, 520, 2  # ragged panels, N not a multiple of the tile
-    mp.spawn(_gather_worker, args=(world, _free_port(), M, N, K, layout, steps, str(tmp_path)), nprocs=world,
-             join=True)
+    spawn_ranks(_gather_worker, lambda port: (world, port, M, N, K, layout, steps, str(tmp_path)), world)
     from oracle import oracle as o
     from tests._util import bits, check_parity, uniform_bf16
     per_rank = [torch.load(os.path.join(tmp_path, f"c{r}.pt")) for r in range(world)]
