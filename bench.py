@@ -699,24 +699,68 @@ def run_shape(args) -> int:
 
 def _config(layout, world):
     return {"workload": "bf16 gemm M=N=K=4096 per GPU, A[M,K] x B[K,N] row-major, U(-1,1), fp32 accumulate, "
-                        "bf16 out; N>1: one 4096-row A panel per rank, B broadcast from rank 0 over NCCL every "
-                        "step, C sharded",
+                        "bf16 out; N>1: one 4096-row A panel per rank, B broadcast from rank 0 every step "
+                        "(copy engines over NVLink, overlapped with the previous step's GEMM), C sharded",
             "M_per_gpu": M_PER_RANK, "N": N_DIM, "K": K_DIM, "b_layout": layout,
             "parallelism": f"row-sharded x{world}" if world > 1 else "single",
             "l2": f"inputs larger than L2: rotating {ROTATE} A/B/C sets ({ROTATE * 96} MiB > 126 MB L2)"}
 
 
-def _step_fn(b200_gemm, A, B, C, layout, world):
-    """One step of the headline job: at N>1 rank 0's B is broadcast (NCCL) to
-    every rank, then every rank multiplies its A panel by it."""
-    import torch.distributed as dist
+class _Steps:
+    """The headline job's steps.  N=1: one GEMM per step.  N>1: step s
+    multiplies this rank's A panel by rank 0's B of step s, delivered by
+    PeerBroadcast (copy engines over NVLink): while the GEMM of step s runs,
+    the B of step s+1 is already moving.  Step numbers count up across warm-up
+    and timed steps (the exchange's flags compare them)."""
 
-    def step(i):
-        j = i % ROTATE
+    def __init__(self, b200_gemm, A, B, C, layout, world, rank, stream):
+        self.g, self.A, self.B, self.C, self.layout = b200_gemm, A, B, C, layout
+        self.world, self.rank, self.stream = world, rank, stream
+        self.s = 0
+        self.pb = None
         if world > 1:
-            dist.broadcast(B[j], src=0)
-        b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
-    return step
+            from b200_gemm.dist import PeerBroadcast
+            nbytes = B[0].numel() * B[0].element_size()
+            self.pb = PeerBroadcast(nbytes)
+            self.slot_views = [None, None]
+            if rank != 0:
+                self.slot_views = [self.pb.data(k).view(torch_bf16()).view(B[0].shape) for k in range(2)]
+            self.pb.issue(0, B[0] if rank == 0 else None)
+
+    def b_of(self, s):
+        return self.B[s % ROTATE] if (self.world == 1 or self.rank == 0) else self.slot_views[s % 2]
+
+    def __call__(self, start_ev=None, end_ev=None):
+        s = self.s
+        self.s += 1
+        j = s % ROTATE
+        if self.pb is not None:
+            self.pb.issue(s + 1, self.B[(s + 1) % ROTATE] if self.rank == 0 else None)
+            self.pb.wait(s, self.stream)
+        if start_ev is not None:
+            start_ev.record(self.stream)
+        self.g.gemm(self.A[j], self.b_of(s), b_layout=self.layout, out=self.C[j])
+        if end_ev is not None:
+            end_ev.record(self.stream)
+        if self.pb is not None:
+            self.pb.release(s, self.stream)
+
+    def exchange_only(self):
+        """One step of the B exchange alone (no GEMM): its cost on its own."""
+        s = self.s
+        self.s += 1
+        self.pb.issue(s + 1, self.B[(s + 1) % ROTATE] if self.rank == 0 else None)
+        self.pb.wait(s, self.stream)
+        self.pb.release(s, self.stream)
+
+    def close(self):
+        if self.pb is not None:
+            self.pb.close()
+
+
+def torch_bf16():
+    import torch
+    return torch.bfloat16
 
 
 def main(argv=None) -> int:
@@ -809,9 +853,9 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         bcast_ms = _max_over_ranks(e0.elapsed_time(e1) / (reps * ROTATE), world)
 
-    step = _step_fn(b200_gemm, A, B, C, layout, world)
+    step = _Steps(b200_gemm, A, B, C, layout, world, rank, stream)
     for i in range(args.warmup):
-        step(i)
+        step()
     torch.cuda.synchronize()
     b200_gemm.check_status()
 
@@ -822,8 +866,8 @@ def main(argv=None) -> int:
     # overlap through programmatic dependent launch: nothing else is put on
     # the stream between them (an event record there would serialise them),
     # so the mean launch duration is the timed region / steps.  At N>1 the
-    # broadcast sits between the GEMMs anyway; there each GEMM is bracketed
-    # by its own events.
+    # exchange's stream waits sit between the GEMMs anyway; there each GEMM
+    # is bracketed by its own events.
     per_launch = world > 1
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if per_launch else []
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if per_launch else []
@@ -834,14 +878,10 @@ def main(argv=None) -> int:
     t_beg.record(stream)
     if per_launch:
         for i in range(args.steps):
-            j = i % ROTATE
-            dist.broadcast(B[j], src=0)
-            starts[i].record(stream)
-            b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
-            ends[i].record(stream)
+            step(starts[i], ends[i])
     else:
         for i in range(args.steps):
-            step(i)
+            step()
     t_end.record(stream)
     torch.cuda.synchronize()
     _barrier(world)
@@ -873,8 +913,16 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         cub_tflops = FLOPS_PER_STEP * n_cub / (c0.elapsed_time(c1) / 1e3) / 1e12
 
+    # ---- N>1: the B exchange checked and timed on its own, and the NCCL
+    # alternative (broadcast, then GEMM, on one stream) in the same run ------
+    exchange = None
+    if world > 1:
+        exchange = _exchange_report(step, A, B, C, layout, world, rank, stream, b200_gemm)
+    step.close()
     # ---- N>1: parity of the sharded result and of the fused all-gather -------
     parity = _multi_gpu_parity(A[0], B[0], layout, world, rank, b200_gemm) if world > 1 else None
+    if parity is not None:
+        parity["b_exchange"] = exchange.pop("bitwise_ok")
     del A, B, C
     torch.cuda.empty_cache()
 
@@ -917,6 +965,8 @@ def main(argv=None) -> int:
         "cublas_same_loop_tflops": round(cub_tflops, 2) if cub_tflops else None,
         "b_broadcast_ms": round(bcast_ms, 4) if bcast_ms is not None else None,
     }
+    if exchange is not None:
+        line["b_exchange"] = exchange
     if parity is not None:
         line["parity"] = parity
     if rowshard is not None:
@@ -931,6 +981,52 @@ def main(argv=None) -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def _exchange_report(step, A, B, C, layout, world, rank, stream, b200_gemm):
+    """After the timed region at N>1: (1) the B that the last step multiplied
+    on every rank equals rank 0's, bit for bit; (2) the exchange alone per
+    step; (3) the design it replaces, NCCL broadcast then GEMM on one stream,
+    per step; device time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    last = step.s - 1
+    torch.cuda.synchronize()
+    ref = B[last % ROTATE].clone() if rank == 0 else torch.empty_like(B[0])
+    dist.broadcast(ref, src=0)
+    torch.cuda.synchronize()
+    ok = torch.tensor([int(torch.equal(step.b_of(last), ref))], device=ref.device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    del ref
+
+    def timed(fn, n=20):
+        for _ in range(3):
+            fn(0)
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        return _max_over_ranks(e0.elapsed_time(e1) / n, world)
+
+    ex_ms = timed(lambda i: step.exchange_only())
+    torch.cuda.synchronize()
+
+    def nccl_step(i):
+        j = i % ROTATE
+        dist.broadcast(B[j], src=0)
+        b200_gemm.gemm(A[j], B[j], b_layout=layout, out=C[j])
+    nccl_ms = timed(nccl_step)
+    b200_gemm.check_status()
+    return {"bitwise_ok": bool(ok.item()),
+            "how": "copy engines (cudaMemcpyAsync into peers' IPC-mapped slots, rank 0 scatters one piece per "
+                   "rank and each rank forwards its piece) with stream-ordered flags between GPUs; no SMs",
+            "exchange_only_ms": round(ex_ms, 4), "nccl_broadcast_then_gemm_ms": round(nccl_ms, 4),
+            "bytes_per_step": B[0].numel() * B[0].element_size()}
 
 
 def _multi_gpu_parity(a, b, layout, world, rank, b200_gemm):

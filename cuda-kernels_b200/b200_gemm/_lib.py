@@ -62,6 +62,9 @@ _SIGNATURES = {
     "b200_ipc_free": (ctypes.c_int, [ctypes.c_void_p]),
     "b200_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     "b200_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "b200_copy_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "b200_signal_u32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
+    "b200_wait_u32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
     "b200_gemm_f32_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_size_t)]),
     "b200_gemm_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

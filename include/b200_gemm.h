@@ -130,6 +130,27 @@ B200_API int b200_ipc_open(const void* handle, void** dev_ptr);
 B200_API int b200_ipc_close(void* dev_ptr);
 
 /*
+ * Copy engines and stream-ordered flags between GPUs, for moving data from
+ * rank to rank over NVLink while a GEMM occupies every SM (a collective
+ * kernel would wait for SMs; these use none).  Peer buffers are mapped with
+ * b200_ipc_open; all calls are asynchronous on `stream`.
+ *   b200_copy_async  cudaMemcpyAsync of `bytes` device to device (either side
+ *                    may be a peer's mapped buffer): the copy engines.
+ *   b200_signal_u32  once all earlier work of `stream` is complete and
+ *                    visible, write `value` to the 4-byte-aligned `flag`
+ *                    (local or a peer's mapped memory).
+ *   b200_wait_u32    later work of `stream` starts once
+ *                    (int32_t)(*flag - value) >= 0 (wrap-aware "flag has
+ *                    reached value"; flags count up by step).
+ * A wait is a stream operation, not a kernel: if its flag is never written
+ * (a peer that stopped), the stream stays blocked until the process exits.
+ * No reference counterpart: the reference has no multi-GPU code.
+ */
+B200_API int b200_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+B200_API int b200_signal_u32(void* flag, uint32_t value, void* stream);
+B200_API int b200_wait_u32(const void* flag, uint32_t value, void* stream);
+
+/*
  * FP32 GEMM, the reference's fp32_matmul operator (fp32_matmul/matmul.cpp:3-9,
  * MatmulFn over float; B stored [K,N] row-major there, B200_B_KN here; [N,K]
  * also accepted): C[M,N] fp32 = A[M,K] fp32 x op(B) fp32, computed on the bf16

@@ -116,3 +116,19 @@ def test_rank_failure_surfaces_as_error(tmp_path):
     err, secs = open(os.path.join(tmp_path, "rank0.txt")).read().split()
     assert err != "None", "broadcast with a missing rank did not raise"
     assert float(secs) < 60
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("nbytes", [16, 1000, 32 << 20, (128 << 20) + 258])
+def test_broadcast_chunks_cover_once_aligned(world, nbytes):
+    """PeerBroadcast's pieces: one per receiving rank, 256-byte aligned starts,
+    together covering the buffer exactly once."""
+    from b200_gemm.dist import broadcast_chunks
+    ch = broadcast_chunks(nbytes, world)
+    assert len(ch) == world - 1
+    pos = 0
+    for off, n in ch:
+        assert off == pos and n >= 0 and (off % 256 == 0 or off == nbytes)
+        pos += n
+    assert pos == nbytes
+    assert broadcast_chunks(nbytes, 1) == []

@@ -118,3 +118,62 @@ def test_gemm_with_fused_allgather(tmp_path, layout):
         check_parity(bits(c0), c32, ref, ctx=f"gather x{world} {layout} step {step}")
         for r in range(1, world):
             assert torch.equal(per_rank[r][step], c0), f"rank {r} gathered a different C at step {step}"
+
+
+def _peer_bcast_worker(rank, world, port, nbytes, steps, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+    import torch.distributed as dist
+    import b200_gemm
+    from b200_gemm.dist import PeerBroadcast
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dev = torch.device("cuda", rank)
+
+        def payload(s):  # the bytes rank 0 sends at step s, reproducible on every rank
+            g = torch.Generator(device=dev).manual_seed(1000 + s)
+            return torch.randint(0, 256, (nbytes,), generator=g, device=dev, dtype=torch.uint8)
+
+        pb = PeerBroadcast(nbytes)
+        stream = torch.cuda.current_stream(dev)
+        srcs = [payload(s) for s in range(steps + 1)] if rank == 0 else None
+        pb.issue(0, srcs[0] if rank == 0 else None)
+        ok = True
+        K = N = 256
+        for s in range(steps):
+            pb.issue(s + 1, srcs[s + 1] if rank == 0 else None)
+            pb.wait(s, stream)
+            got = pb.data(s, srcs[s] if rank == 0 else None)
+            ok &= bool(torch.equal(got, payload(s)))  # on `stream`, after the wait
+            # a GEMM reading the delivered bytes as B [K, N] (the bench's use)
+            a = torch.ones((64, K), dtype=torch.bfloat16, device=dev)
+            bmat = got[:K * N * 2].view(torch.bfloat16).view(K, N)
+            c = b200_gemm.gemm(a, bmat, b_layout="kn")
+            ref = b200_gemm.gemm(a, payload(s)[:K * N * 2].view(torch.bfloat16).view(K, N), b_layout="kn")
+            ok &= bool(torch.equal(torch.nan_to_num(c, nan=0.0), torch.nan_to_num(ref, nan=0.0)))
+            pb.release(s, stream)
+        torch.cuda.synchronize()
+        pb.close()
+        assert b200_gemm.check_status() == 0
+        flag = torch.tensor([int(ok)], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if rank == 0:
+            torch.save(bool(flag.item()), os.path.join(result_dir, "ok.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nbytes", [(2 << 20) + 258, 32 << 20])
+def test_peer_broadcast_delivers_every_step(tmp_path, nbytes):
+    """PeerBroadcast (copy engines + stream-ordered flags): over several steps,
+    with two receive slots reused in turn, every rank receives exactly the
+    bytes rank 0 sent for that step, and a GEMM reading them on the same
+    stream sees them."""
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(world, 8)
+    spawn_ranks(_peer_bcast_worker, lambda port: (world, port, nbytes, 7, str(tmp_path)), world)
+    assert torch.load(os.path.join(tmp_path, "ok.pt"))
