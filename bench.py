@@ -862,26 +862,21 @@ def main(argv=None) -> int:
     props = torch.cuda.get_device_properties(dev)
     sampler = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
     t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # At N=1 a step is exactly one GEMM launch, and consecutive launches
-    # overlap through programmatic dependent launch: nothing else is put on
-    # the stream between them (an event record there would serialise them),
-    # so the mean launch duration is the timed region / steps.  At N>1 the
-    # exchange's stream waits sit between the GEMMs anyway; there each GEMM
-    # is bracketed by its own events.
-    per_launch = world > 1
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if per_launch else []
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if per_launch else []
+    # A step is exactly one GEMM launch (plus, at N>1, the exchange's stream
+    # operations), and consecutive launches overlap through programmatic
+    # dependent launch: no event is put on the stream between them (an event
+    # record there serialises them, ~3 us a step), so the mean launch
+    # duration is taken as the timed region / steps (at N>1 an upper bound
+    # that includes the exchange's waits).
 
     _barrier(world)
     torch.cuda.synchronize()
     sampler.start()
     t_beg.record(stream)
-    if per_launch:
-        for i in range(args.steps):
-            step(starts[i], ends[i])
-    else:
-        for i in range(args.steps):
-            step()
+    h0 = time.perf_counter()
+    for i in range(args.steps):
+        step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to enqueue one step
     t_end.record(stream)
     torch.cuda.synchronize()
     _barrier(world)
@@ -889,11 +884,9 @@ def main(argv=None) -> int:
     b200_gemm.check_status()
 
     total_ms = _max_over_ranks(t_beg.elapsed_time(t_end), world)
-    if per_launch:
-        launch_ms = statistics.fmean(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
-    else:
-        launch_ms = t_beg.elapsed_time(t_end) / args.steps
+    launch_ms = t_beg.elapsed_time(t_end) / args.steps
     launch_ms_max = _max_over_ranks(launch_ms, world)
+    host_ms_max = _max_over_ranks(host_ms, world)
     tflops = world * FLOPS_PER_STEP * args.steps / (total_ms / 1e3) / 1e12
     kernel_tflops = FLOPS_PER_STEP / (launch_ms_max / 1e3) / 1e12
 
@@ -957,8 +950,8 @@ def main(argv=None) -> int:
                      "traffic": (traffic or {}).get("bytes_per_launch"),
                      "algorithmic_flops_per_launch": FLOPS_PER_STEP,
                      "avg_launch_ms": round(launch_ms_max, 5),
-                     "launch_timing": ("events around each GEMM launch (max over ranks)" if per_launch else
-                                       "timed region / steps: one GEMM launch per step, back to back")},
+                     "launch_timing": "timed region / steps: one GEMM launch per step, back to back (max over ranks)"},
+        "host_enqueue_ms_per_step": round(host_ms_max, 4),
         "clocks": sampler.summary(),
         "gpu_launches": args.steps,
         "e2e": e2e,
