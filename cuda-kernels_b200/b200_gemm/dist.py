@@ -243,14 +243,16 @@ class PeerBroadcast:
     2 GPUs, 32 MiB of B per 4096^3 step: broadcast then GEMM 156 us a step,
     NCCL on a side stream 119 us, copy engines 100 us against 95 us for the
     GEMM alone).  Here every rank owns two IPC-mapped receive slots (step s
-    uses slot s % 2) and a small flag array; rank 0 scatters piece q of the
-    buffer to rank q+1 (broadcast_chunks), and each receiving rank forwards
-    its piece to the other receivers as soon as it has landed, so every byte
-    crosses rank 0's links once.  Copies are cudaMemcpyAsync into the peers'
-    slots (b200_copy_async), each followed by a flag write into the reader's
-    memory (b200_signal_u32); a reader's compute stream waits for its flags
-    (b200_wait_u32) before the GEMM of that step, and after the GEMM tells
-    every writer that the slot is free again.  No SM is used by any of it.
+    uses slot s % 2) and a small flag array; rank 0 scatters piece q-1 of the
+    buffer to rank q (broadcast_chunks), and each receiving rank forwards its
+    piece to the other receivers as soon as it has landed, so every byte
+    crosses rank 0's links once.  Copies go into the peers' slots on the copy
+    engines, each followed by a flag write into the reader's memory; a
+    reader's compute stream waits for its flags before the GEMM of that step,
+    and after the GEMM tells every writer that the slot is free again.  No SM
+    is used by any of it.  The per-step protocol is native (b200_bcast_* in
+    include/b200_gemm.h): a step costs three calls whatever the world size.
+    This class allocates and maps the buffers and exchanges their handles.
 
     Per step s, on every rank, in the same order:
         pb.issue(s + 1, src)      # rank 0: the next step's buffer (others: None)
@@ -274,14 +276,14 @@ class PeerBroadcast:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("PeerBroadcast supports up to 8 ranks")
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        self.chunks = broadcast_chunks(self.nbytes, self.world)
         W = self.world
-        self._flag_bytes = max(4 * (self.SLOTS * W + W), 16)
-        own = []
-        handles = []
+        flag_bytes = max(int(self._lib.b200_bcast_flag_bytes(W)), 16)
+        own, handles = [], []
         with torch.cuda.device(self.device):
-            for nb in [self.nbytes] * self.SLOTS + [self._flag_bytes]:
+            for nb in [self.nbytes] * self.SLOTS + [flag_bytes]:
                 p = ctypes.c_void_p()
                 h = (ctypes.c_ubyte * _lib.B200_IPC_HANDLE_BYTES)()
                 rc = self._lib.b200_ipc_alloc(max(nb, 16), ctypes.byref(p), ctypes.cast(h, ctypes.c_void_p))
@@ -290,118 +292,78 @@ class PeerBroadcast:
                 own.append(p.value)
                 handles.append(bytes(h))
         self._own = own
-        self.slot_ptr = own[:self.SLOTS]
-        self.flag_ptr = own[self.SLOTS]
-        flags = torch.as_tensor(_DevBuf(self.flag_ptr, (self._flag_bytes // 2,)), device=self.device)
+        flags = torch.as_tensor(_DevBuf(own[self.SLOTS], ((flag_bytes + 1) // 2,)), device=self.device)
         flags.zero_()
         torch.cuda.synchronize(self.device)
         all_h = [None] * W
         dist.all_gather_object(all_h, handles, group=group)
         self._opened = []
-        self.peer_slot = {}
-        self.peer_flag = {}
+        ptrs = {self.rank: own}
         with torch.cuda.device(self.device):
             for r in range(W):
                 if r == self.rank:
                     continue
-                ptrs = []
+                mapped = []
                 for h in all_h[r]:
                     hb = (ctypes.c_ubyte * _lib.B200_IPC_HANDLE_BYTES).from_buffer_copy(h)
                     pp = ctypes.c_void_p()
                     rc = self._lib.b200_ipc_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(pp))
                     if rc != _lib.B200_OK:
                         raise _lib.B200GemmError(rc, f"b200_ipc_open(rank {r})")
-                    ptrs.append(pp.value)
+                    mapped.append(pp.value)
                     self._opened.append(pp.value)
-                self.peer_slot[r] = ptrs[:self.SLOTS]
-                self.peer_flag[r] = ptrs[self.SLOTS]
+                ptrs[r] = mapped
+        slots = (ctypes.c_void_p * (W * self.SLOTS))(*[ptrs[r][k] for r in range(W) for k in range(self.SLOTS)])
+        flagp = (ctypes.c_void_p * W)(*[ptrs[r][self.SLOTS] for r in range(W)])
+        handle = ctypes.c_void_p()
+        rc = self._lib.b200_bcast_create(self.rank, W, self.nbytes, slots, flagp, ctypes.byref(handle))
+        if rc != _lib.B200_OK:
+            raise _lib.B200GemmError(rc, "b200_bcast_create")
+        self._h = handle
+        self.slot_ptr = own[:self.SLOTS]
         self.comm = torch.cuda.Stream(self.device)
         self._copied = [torch.cuda.Event() for _ in range(self.SLOTS)]
         dist.barrier(group=group)  # every rank's flags are zero before anyone signals
-
-    # flag layout (uint32): ready[slot][sender], then done[rank]
-    def _ready(self, base: int, slot: int, sender: int) -> int:
-        return base + 4 * (slot * self.world + sender)
-
-    def _done(self, base: int, r: int) -> int:
-        return base + 4 * (self.SLOTS * self.world + r)
 
     def _check(self, rc: int, what: str) -> None:
         from . import _lib
         if rc != _lib.B200_OK:
             raise _lib.B200GemmError(rc, what)
 
-    def _copy(self, dst: int, src: int, n: int, stream) -> None:
-        import ctypes
-        self._check(self._lib.b200_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), n,
-                                              ctypes.c_void_p(stream.cuda_stream)), "b200_copy_async")
-
-    def _signal(self, flag: int, value: int, stream) -> None:
-        import ctypes
-        self._check(self._lib.b200_signal_u32(ctypes.c_void_p(flag), value & 0xFFFFFFFF,
-                                              ctypes.c_void_p(stream.cuda_stream)), "b200_signal_u32")
-
-    def _wait(self, flag: int, value: int, stream) -> None:
-        import ctypes
-        self._check(self._lib.b200_wait_u32(ctypes.c_void_p(flag), value & 0xFFFFFFFF,
-                                            ctypes.c_void_p(stream.cuda_stream)), "b200_wait_u32")
-
     def issue(self, step: int, src: torch.Tensor | None = None) -> None:
         """Queue the copies of step `step` on the copy stream (rank 0: from `src`,
         a contiguous tensor of nbytes on this device; others: forwarding)."""
+        import ctypes
         if self.world == 1:
             return
-        slot = step % self.SLOTS
-        v = step + 1
-        c = self.comm
+        ptr = None
         if self.rank == 0:
             if src is None or not src.is_contiguous() or src.numel() * src.element_size() != self.nbytes:
                 raise ValueError("rank 0 needs a contiguous source tensor of nbytes")
-            base = src.data_ptr()
-            for q in range(1, self.world):
-                off, n = self.chunks[q - 1]
-                if step >= self.SLOTS:  # q is done with the step that last used this slot
-                    self._wait(self._done(self.flag_ptr, q), step - self.SLOTS + 1, c)
-                self._copy(self.peer_slot[q][slot] + off, base + off, n, c)
-                self._signal(self._ready(self.peer_flag[q], slot, 0), v, c)
-            self._copied[slot].record(c)
-            return
-        # receiving rank: wait for my piece from rank 0, then forward it
-        off, n = self.chunks[self.rank - 1]
-        self._wait(self._ready(self.flag_ptr, slot, 0), v, c)
-        mine = self.slot_ptr[slot] + off
-        for r in range(1, self.world):
-            if r == self.rank:
-                continue
-            if step >= self.SLOTS:
-                self._wait(self._done(self.flag_ptr, r), step - self.SLOTS + 1, c)
-            self._copy(self.peer_slot[r][slot] + off, mine, n, c)
-            self._signal(self._ready(self.peer_flag[r], slot, self.rank), v, c)
+            ptr = src.data_ptr()
+        self._check(self._lib.b200_bcast_issue(self._h, step, ctypes.c_void_p(ptr),
+                                               ctypes.c_void_p(self.comm.cuda_stream)), "b200_bcast_issue")
+        if self.rank == 0:
+            self._copied[step % self.SLOTS].record(self.comm)
 
     def wait(self, step: int, stream) -> None:
         """Make `stream` wait until this rank's slot of `step` is complete."""
-        if self.world == 1 or self.rank == 0:
-            return
-        slot = step % self.SLOTS
-        for r in range(self.world):
-            if r != self.rank:
-                self._wait(self._ready(self.flag_ptr, slot, r), step + 1, stream)
+        import ctypes
+        self._check(self._lib.b200_bcast_wait(self._h, step, ctypes.c_void_p(stream.cuda_stream)), "b200_bcast_wait")
 
     def data(self, step: int, src: torch.Tensor | None = None) -> torch.Tensor:
         """The buffer of `step` on this rank as flat bytes (rank 0: src itself)."""
         if self.rank == 0 or self.world == 1:
             return src
         p = self.slot_ptr[step % self.SLOTS]
-        return torch.as_tensor(_DevBuf(p, (self.nbytes // 2,)), device=self.device).view(torch.uint8)[:self.nbytes]
+        return torch.as_tensor(_DevBuf(p, ((self.nbytes + 1) // 2,)), device=self.device).view(torch.uint8)[:self.nbytes]
 
     def release(self, step: int, stream) -> None:
         """After the work on `stream` that reads slot `step` % 2: tell every
         rank that writes into this rank's slots that it may overwrite it."""
-        if self.world == 1 or self.rank == 0:
-            return
-        for r in range(self.world):
-            if r != self.rank:
-                self._signal(self._done(self.peer_flag[r], self.rank), step + 1, stream)
+        import ctypes
+        self._check(self._lib.b200_bcast_release(self._h, step, ctypes.c_void_p(stream.cuda_stream)),
+                    "b200_bcast_release")
 
     def copied(self, step: int) -> "torch.cuda.Event":
         """Rank 0: event after its copies of `step` (src may change once it has completed)."""
@@ -414,6 +376,7 @@ class PeerBroadcast:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
+        self._lib.b200_bcast_destroy(self._h)
         with torch.cuda.device(self.device):
             for p in self._opened:
                 self._lib.b200_ipc_close(p)

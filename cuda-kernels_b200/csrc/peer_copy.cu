@@ -19,6 +19,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <new>
 
 #include "b200_gemm.h"
 
@@ -77,4 +78,137 @@ extern "C" B200_API int b200_wait_u32(const void* flag, uint32_t value, void* st
   const CUresult r = g_wait32(reinterpret_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(const_cast<void*>(flag)),
                               value, CU_STREAM_WAIT_VALUE_GEQ);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Per-step broadcast from rank 0 over the copy engines (b200_bcast_*): the
+// protocol the multi-GPU driver runs every step, in native code so that a
+// step costs three calls however many ranks there are.
+//
+// Every rank owns kSlots receive slots of `nbytes` (step s uses slot
+// s % kSlots) and a flag array, all mapped by every peer (CUDA IPC).  Flags
+// (uint32): ready[slot][sender] — the sender's piece of that slot has landed
+// (value step + 1); done[rank] — that rank has finished reading its slot of
+// a step (value step + 1).  Pieces: the buffer is cut into world - 1 pieces
+// (b200_bcast_piece); rank 0 sends piece q-1 to rank q, and rank q forwards
+// it to every other receiving rank once it has landed, so every byte leaves
+// rank 0 once.  Before writing into a peer's slot for step s, a writer waits
+// until that peer is done with step s - kSlots, which used the same slot.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kBcastSlots = 2;
+constexpr int kBcastMaxWorld = 8;
+}  // namespace
+
+struct b200_bcast {
+  int rank, world;
+  size_t nbytes;
+  char* slot[kBcastMaxWorld][kBcastSlots];  // every rank's slots as mapped in this process
+  char* flags[kBcastMaxWorld];              // every rank's flag array as mapped in this process
+};
+
+namespace {
+inline uint32_t* ready_flag(const b200_bcast* b, int owner, int slot, int sender) {
+  return reinterpret_cast<uint32_t*>(b->flags[owner]) + slot * b->world + sender;
+}
+inline uint32_t* done_flag(const b200_bcast* b, int owner, int r) {
+  return reinterpret_cast<uint32_t*>(b->flags[owner]) + kBcastSlots * b->world + r;
+}
+}  // namespace
+
+extern "C" B200_API int b200_bcast_piece(int world, size_t nbytes, int index, size_t* offset, size_t* length) {
+  if (offset == nullptr || length == nullptr || world < 2 || index < 0 || index >= world - 1)
+    return B200_ERR_INVALID_ARG;
+  const size_t parts = (size_t)(world - 1);
+  auto bound = [&](size_t i) -> size_t {
+    if (i >= parts) return nbytes;
+    size_t b = (nbytes * i / parts + 255) / 256 * 256;
+    return b < nbytes ? b : nbytes;
+  };
+  *offset = bound((size_t)index);
+  *length = bound((size_t)index + 1) - *offset;
+  return B200_OK;
+}
+
+extern "C" B200_API size_t b200_bcast_flag_bytes(int world) {
+  return (size_t)(kBcastSlots * world + world) * sizeof(uint32_t);
+}
+
+extern "C" B200_API int b200_bcast_create(int rank, int world, size_t nbytes, void* const* slots, void* const* flags,
+                                          b200_bcast** out) {
+  if (out == nullptr || slots == nullptr || flags == nullptr) return B200_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (world < 1 || world > kBcastMaxWorld || rank < 0 || rank >= world) return B200_ERR_INVALID_ARG;
+  b200_bcast* b = new (std::nothrow) b200_bcast{};
+  if (b == nullptr) return B200_ERR_CUDA;
+  b->rank = rank;
+  b->world = world;
+  b->nbytes = nbytes;
+  for (int r = 0; r < world; ++r) {
+    for (int k = 0; k < kBcastSlots; ++k) b->slot[r][k] = static_cast<char*>(slots[r * kBcastSlots + k]);
+    b->flags[r] = static_cast<char*>(flags[r]);
+    if (b->flags[r] == nullptr || !aligned4(b->flags[r])) {
+      delete b;
+      return B200_ERR_INVALID_ARG;
+    }
+  }
+  *out = b;
+  return B200_OK;
+}
+
+extern "C" B200_API void b200_bcast_destroy(b200_bcast* b) { delete b; }
+
+extern "C" B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void* src, void* stream) {
+  if (b == nullptr || step < 0) return B200_ERR_INVALID_ARG;
+  if (b->world == 1) return B200_OK;
+  const int slot = (int)(step % kBcastSlots);
+  const uint32_t v = (uint32_t)(step + 1);
+  const bool reuse = step >= kBcastSlots;  // the slot held step - kSlots: wait until its reader is done
+  const uint32_t v_prev = (uint32_t)(step - kBcastSlots + 1);
+  int rc;
+  if (b->rank == 0) {
+    if (src == nullptr) return B200_ERR_INVALID_ARG;
+    for (int q = 1; q < b->world; ++q) {
+      size_t off, len;
+      if ((rc = b200_bcast_piece(b->world, b->nbytes, q - 1, &off, &len)) != B200_OK) return rc;
+      if (reuse && (rc = b200_wait_u32(done_flag(b, 0, q), v_prev, stream)) != B200_OK) return rc;
+      if ((rc = b200_copy_async(b->slot[q][slot] + off, static_cast<const char*>(src) + off, len, stream)) != B200_OK)
+        return rc;
+      if ((rc = b200_signal_u32(ready_flag(b, q, slot, 0), v, stream)) != B200_OK) return rc;
+    }
+    return B200_OK;
+  }
+  size_t off, len;
+  if ((rc = b200_bcast_piece(b->world, b->nbytes, b->rank - 1, &off, &len)) != B200_OK) return rc;
+  if ((rc = b200_wait_u32(ready_flag(b, b->rank, slot, 0), v, stream)) != B200_OK) return rc;  // my piece is here
+  for (int r = 1; r < b->world; ++r) {
+    if (r == b->rank) continue;
+    if (reuse && (rc = b200_wait_u32(done_flag(b, b->rank, r), v_prev, stream)) != B200_OK) return rc;
+    if ((rc = b200_copy_async(b->slot[r][slot] + off, b->slot[b->rank][slot] + off, len, stream)) != B200_OK) return rc;
+    if ((rc = b200_signal_u32(ready_flag(b, r, slot, b->rank), v, stream)) != B200_OK) return rc;
+  }
+  return B200_OK;
+}
+
+extern "C" B200_API int b200_bcast_wait(b200_bcast* b, int64_t step, void* stream) {
+  if (b == nullptr || step < 0) return B200_ERR_INVALID_ARG;
+  if (b->world == 1 || b->rank == 0) return B200_OK;
+  const int slot = (int)(step % kBcastSlots);
+  for (int r = 0; r < b->world; ++r) {
+    if (r == b->rank) continue;
+    const int rc = b200_wait_u32(ready_flag(b, b->rank, slot, r), (uint32_t)(step + 1), stream);
+    if (rc != B200_OK) return rc;
+  }
+  return B200_OK;
+}
+
+extern "C" B200_API int b200_bcast_release(b200_bcast* b, int64_t step, void* stream) {
+  if (b == nullptr || step < 0) return B200_ERR_INVALID_ARG;
+  if (b->world == 1 || b->rank == 0) return B200_OK;
+  for (int r = 0; r < b->world; ++r) {
+    if (r == b->rank) continue;
+    const int rc = b200_signal_u32(done_flag(b, r, b->rank), (uint32_t)(step + 1), stream);
+    if (rc != B200_OK) return rc;
+  }
+  return B200_OK;
 }

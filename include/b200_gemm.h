@@ -151,6 +151,38 @@ B200_API int b200_signal_u32(void* flag, uint32_t value, void* stream);
 B200_API int b200_wait_u32(const void* flag, uint32_t value, void* stream);
 
 /*
+ * Per-step broadcast of one buffer from rank 0 to every rank, built on the
+ * three calls above (the multi-GPU driver's B exchange; one process per GPU,
+ * world <= 8).  Every rank owns two receive slots of `nbytes` (step s uses
+ * slot s % 2) and a flag array of b200_bcast_flag_bytes(world) bytes, zeroed
+ * before first use; all of them are mapped in every process (b200_ipc_*).
+ * Rank 0 sends piece q-1 (b200_bcast_piece: world-1 pieces, 256-byte
+ * aligned) to rank q, and rank q forwards its piece to the other receiving
+ * ranks once it has landed, so every byte leaves rank 0 once.
+ *   b200_bcast_create   slots[r * 2 + k] = rank r's slot k and flags[r] =
+ *                       rank r's flags, as mapped in this process.
+ *   b200_bcast_issue    queue step `step`'s copies on `stream` (rank 0 from
+ *                       `src`; the others forward); every rank calls it.
+ *   b200_bcast_wait     `stream` waits until this rank's slot of `step` is
+ *                       complete (no-op on rank 0, which reads src).
+ *   b200_bcast_release  after the work on `stream` that reads the slot of
+ *                       `step`: its writers may overwrite it two steps on.
+ * Steps count up from 0 on every rank, each call made by every rank in the
+ * same order.  No SMs are used.  A rank that stops calling leaves the
+ * others' streams waiting (no time limit, see b200_wait_u32).
+ * No reference counterpart: the reference has no multi-GPU code.
+ */
+typedef struct b200_bcast b200_bcast;
+B200_API int b200_bcast_piece(int world, size_t nbytes, int index, size_t* offset, size_t* length);
+B200_API size_t b200_bcast_flag_bytes(int world);
+B200_API int b200_bcast_create(int rank, int world, size_t nbytes, void* const* slots, void* const* flags,
+                               b200_bcast** out);
+B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void* src, void* stream);
+B200_API int b200_bcast_wait(b200_bcast* b, int64_t step, void* stream);
+B200_API int b200_bcast_release(b200_bcast* b, int64_t step, void* stream);
+B200_API void b200_bcast_destroy(b200_bcast* b);
+
+/*
  * FP32 GEMM, the reference's fp32_matmul operator (fp32_matmul/matmul.cpp:3-9,
  * MatmulFn over float; B stored [K,N] row-major there, B200_B_KN here; [N,K]
  * also accepted): C[M,N] fp32 = A[M,K] fp32 x op(B) fp32, computed on the bf16

@@ -156,3 +156,23 @@ def test_f32_argument_errors_without_gpu():
     assert lib.b200_gemm_f32(fake, fake, P(0x10004), 8, 8, 8, 8, 8, 8, 1, fake, 1 << 20, None) == _lib.B200_ERR_ALIGNMENT
     assert lib.b200_gemm_f32(fake, fake, fake, 8, 8, 8, 8, 8, 8, 1, fake, 16, None) == _lib.B200_ERR_INVALID_ARG
     assert lib.b200_gemm_f32(fake, fake, fake, 8, 8, 8, 8, 8, 8, 1, P(0x10010), 1 << 20, None) == _lib.B200_ERR_ALIGNMENT
+
+
+def test_bcast_pieces_match_the_documented_layout():
+    """b200_bcast_piece (native, host only) cuts the buffer exactly as
+    dist.broadcast_chunks documents: world-1 pieces, 256-byte aligned starts."""
+    import ctypes
+    from b200_gemm import _lib
+    from b200_gemm.dist import broadcast_chunks
+    lib = _lib.load()
+    for world in (2, 3, 5, 8):
+        for nbytes in (16, 1000, 32 << 20, (128 << 20) + 258):
+            got = []
+            for i in range(world - 1):
+                off, n = ctypes.c_size_t(), ctypes.c_size_t()
+                assert lib.b200_bcast_piece(world, nbytes, i, ctypes.byref(off), ctypes.byref(n)) == _lib.B200_OK
+                got.append((off.value, n.value))
+            assert got == broadcast_chunks(nbytes, world)
+    off, n = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.b200_bcast_piece(1, 100, 0, ctypes.byref(off), ctypes.byref(n)) == _lib.B200_ERR_INVALID_ARG
+    assert lib.b200_bcast_flag_bytes(8) == 4 * (2 * 8 + 8)
