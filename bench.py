@@ -730,20 +730,17 @@ class _Steps:
     def b_of(self, s):
         return self.B[s % ROTATE] if (self.world == 1 or self.rank == 0) else self.slot_views[s % 2]
 
-    def __call__(self, start_ev=None, end_ev=None):
+    def __call__(self):
         s = self.s
         self.s += 1
         j = s % ROTATE
-        if self.pb is not None:
-            self.pb.issue(s + 1, self.B[(s + 1) % ROTATE] if self.rank == 0 else None)
-            self.pb.wait(s, self.stream)
-        if start_ev is not None:
-            start_ev.record(self.stream)
-        self.g.gemm(self.A[j], self.b_of(s), b_layout=self.layout, out=self.C[j])
-        if end_ev is not None:
-            end_ev.record(self.stream)
-        if self.pb is not None:
-            self.pb.release(s, self.stream)
+        if self.pb is None:
+            self.g.gemm(self.A[j], self.B[j], b_layout=self.layout, out=self.C[j])
+            return
+        self.pb.issue(s + 1, self.B[(s + 1) % ROTATE] if self.rank == 0 else None)
+        # waits for this step's B and releases its slot inside the GEMM kernel
+        self.pb.gemm(s, self.A[j], tuple(self.B[0].shape), out=self.C[j], b_layout=self.layout,
+                     src=self.B[j] if self.rank == 0 else None, stream=self.stream)
 
     def exchange_only(self):
         """One step of the B exchange alone (no GEMM): its cost on its own."""

@@ -74,6 +74,10 @@ _SIGNATURES = {
     "b200_bcast_wait": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     "b200_bcast_release": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     "b200_bcast_destroy": (None, [ctypes.c_void_p]),
+    "b200_bcast_gemm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                       ctypes.c_void_p]),
     "b200_gemm_f32_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_size_t)]),
     "b200_gemm_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

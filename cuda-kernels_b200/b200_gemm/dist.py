@@ -365,6 +365,31 @@ class PeerBroadcast:
         self._check(self._lib.b200_bcast_release(self._h, step, ctypes.c_void_p(stream.cuda_stream)),
                     "b200_bcast_release")
 
+    def gemm(self, step: int, a: torch.Tensor, b_shape, *, out: torch.Tensor, b_layout: str = "kn",
+             src: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """out = a @ op(B of step `step`) through b200_bcast_gemm, in place of
+        wait / gemm / release: the CTA-pair kernel waits for the step's data and
+        releases the slot itself, so consecutive GEMMs on `stream` keep their
+        programmatic overlap.  b_shape is B's shape as rank 0 holds it (rank 0
+        passes its B as `src`)."""
+        import ctypes
+        from . import _lib
+        stream = stream if stream is not None else torch.cuda.current_stream(self.device)
+        M, K = a.shape
+        rows, cols = b_shape
+        N = rows if b_layout == "nk" else cols
+        if (cols if b_layout == "nk" else rows) != K or tuple(out.shape) != (M, N):
+            raise ValueError("shapes of A, B and out do not match")
+        if a.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or a.stride(1) != 1 or out.stride(1) != 1:
+            raise ValueError("A and out must be row-major bf16")
+        b0 = src.data_ptr() if (self.rank == 0 and src is not None) else None
+        rc = self._lib.b200_bcast_gemm(self._h, step, ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b0),
+                                       ctypes.c_void_p(out.data_ptr()), M, N, K, max(a.stride(0), 1), cols,
+                                       max(out.stride(0), 1), _lib.B200_B_NK if b_layout == "nk" else _lib.B200_B_KN,
+                                       ctypes.c_void_p(stream.cuda_stream))
+        self._check(rc, f"b200_bcast_gemm step {step}")
+        return out
+
     def copied(self, step: int) -> "torch.cuda.Event":
         """Rank 0: event after its copies of `step` (src may change once it has completed)."""
         return self._copied[step % self.SLOTS]

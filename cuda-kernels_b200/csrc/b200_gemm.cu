@@ -24,6 +24,7 @@
 #include "gemm_sm100_skinny.cuh"
 #include "split_f32.cuh"
 #include "attn_sm100.cuh"
+#include "peer_bcast.h"
 
 namespace {
 
@@ -394,6 +395,34 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
 
 namespace {
 
+// The exchange's dependencies of one GEMM (b200_bcast_gemm): flags in this
+// GPU's memory that must reach dep_value before B may be read, and flags in
+// the writers' memory that get rel_value once B is no longer read.
+struct PeerHooks {
+  const uint32_t* dep[b200::kBcastMaxWorld];
+  uint32_t* rel[b200::kBcastMaxWorld];
+  uint32_t* counter;  // this GPU's count of CTA pairs done reading (pair kernel)
+  int n_dep, n_rel;
+  uint32_t dep_value, rel_value;
+};
+
+// Kernels without the in-kernel hooks take them as stream operations around
+// the launch (the wait before, the release after).
+int hooks_before(const PeerHooks* h, cudaStream_t stream) {
+  for (int i = 0; h != nullptr && i < h->n_dep; ++i) {
+    const int rc = b200_wait_u32(h->dep[i], h->dep_value, stream);
+    if (rc != B200_OK) return rc;
+  }
+  return B200_OK;
+}
+int hooks_after(const PeerHooks* h, cudaStream_t stream) {
+  for (int i = 0; h != nullptr && i < h->n_rel; ++i) {
+    const int rc = b200_signal_u32(h->rel[i], h->rel_value, stream);
+    if (rc != B200_OK) return rc;
+  }
+  return B200_OK;
+}
+
 // `epi` == nullptr: plain GEMM, C = bf16(A op(B)).  Otherwise a validated
 // fused epilogue (see b200_gemm_bf16_ex); C is then D, of its element type.
 // M > 128 problems so small that 256 x 256 CTA-pair tiles would occupy at
@@ -408,9 +437,13 @@ inline bool use_small_tiles(const DeviceState& st, int64_t M, int64_t N) {
 
 // `outs` != nullptr: the gathering GEMM (b200_gemm_bf16_allgather): CTA-pair
 // 256 x 256 tiles, every tile stored through each of outs->m[0 .. n_out).
+// `hooks` != nullptr (M, N, K >= 1, no workspace): B is an exchange slot
+// (b200_bcast_gemm); the pair kernel waits and releases inside, the others
+// get stream operations around their launch.
 int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
               int64_t ldc, int b_layout, void* workspace, size_t workspace_bytes, void* stream_,
-              const b200::EpilogueParams* epi_in = nullptr, const b200::OutMaps* outs = nullptr, int n_out = 1) {
+              const b200::EpilogueParams* epi_in = nullptr, const b200::OutMaps* outs = nullptr, int n_out = 1,
+              const PeerHooks* hooks = nullptr) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARG;
   if (b_layout != B200_B_NK && b_layout != B200_B_KN) return B200_ERR_INVALID_ARG;
   const int64_t kLim = 0x7fffffffLL;
@@ -449,10 +482,12 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
   const int force = outs != nullptr ? kForcePair : g_force_kernel.load(std::memory_order_relaxed);
   if (force == kForceSkinny && M > 128) return B200_ERR_INVALID_ARG;
   if (force == kForceSkinny || (force == kForceAuto && M <= 128)) {
-    if (M <= 16) return launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
-    if (M <= 32) return launch_skinny<32>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
-    if (M <= 64) return launch_skinny<64>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
-    return launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    if ((rc = hooks_before(hooks, stream)) != B200_OK) return rc;
+    if (M <= 16) rc = launch_skinny<16>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    else if (M <= 32) rc = launch_skinny<32>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    else if (M <= 64) rc = launch_skinny<64>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    else rc = launch_skinny<128>(*st, A, B, C, M, N, K, lda, ldb, ldc, b_layout, epi, stream);
+    return rc == B200_OK ? hooks_after(hooks, stream) : rc;
   }
   const bool use_small = force == kForceAuto && use_small_tiles(*st, M, N);
   const bool use_pair = force == kForcePair || (force == kForceAuto && M > b200::kBM && !use_small);
@@ -553,7 +588,9 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+    if ((rc = hooks_before(hooks, stream)) != B200_OK) return rc;
+    if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p) != cudaSuccess) return B200_ERR_CUDA;
+    return hooks_after(hooks, stream);
   }
   p.sk_first = p.num_tiles;
   p.sk_parts = 1;
@@ -575,6 +612,17 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
       const uint32_t n = st->epoch.fetch_add(1, std::memory_order_relaxed) + 1;
       p.epoch = ((uint64_t)process_salt() << 32) | (uint64_t)n;
     }
+  }
+  if (hooks != nullptr) {
+    // In the kernel: every producer waits for the dep flags before its first
+    // load of B, and the last CTA pair to finish loading writes the releases.
+    for (int i = 0; i < hooks->n_dep; ++i) p.dep_flags[i] = hooks->dep[i];
+    for (int i = 0; i < hooks->n_rel; ++i) p.rel_flags[i] = hooks->rel[i];
+    p.n_dep = hooks->n_dep;
+    p.n_rel = hooks->n_rel;
+    p.dep_value = hooks->dep_value;
+    p.rel_value = hooks->rel_value;
+    p.rel_counter = hooks->counter;
   }
   const int64_t work = p.num_work;
   const int pairs = (int)(work < max_pairs ? work : max_pairs);
@@ -622,6 +670,35 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
 extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                                        int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream) {
   return gemm_impl(A, B, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
+}
+
+extern "C" B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, const void* A, const void* B0, void* C,
+                                        int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                        int b_layout, void* stream) {
+  if (b == nullptr || step < 0) return B200_ERR_INVALID_ARG;
+  if (b->world == 1 || b->rank == 0) return gemm_impl(A, B0, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
+  if (M < 0 || N < 0 || K < 0 || b_layout < B200_B_NK || b_layout > B200_B_KN) return B200_ERR_INVALID_ARG;
+  const int64_t b_rows = b_layout == B200_B_NK ? N : K;
+  if (b_rows > 0 && ((uint64_t)(b_rows - 1) * (uint64_t)ldb + (uint64_t)(b_layout == B200_B_NK ? K : N)) * 2 >
+                        (uint64_t)b->nbytes)
+    return B200_ERR_INVALID_ARG;  // B would run past this rank's slot
+  const int slot = (int)(step % b200::kBcastSlots);
+  PeerHooks h{};
+  for (int r = 0; r < b->world; ++r) {
+    if (r == b->rank) continue;
+    h.dep[h.n_dep++] = b200::bcast_ready(b, b->rank, slot, r);  // every piece of this step's slot has landed
+    h.rel[h.n_rel++] = b200::bcast_done(b, r, b->rank);        // each writer: this rank is done with the slot
+  }
+  h.counter = b200::bcast_counter(b);
+  h.dep_value = h.rel_value = (uint32_t)(step + 1);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0 || K == 0) {  // nothing reads B: keep the protocol with stream operations
+    int rc = hooks_before(&h, s);
+    if (rc == B200_OK) rc = gemm_impl(A, b->slot[b->rank][slot], C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
+    return rc == B200_OK ? hooks_after(&h, s) : rc;
+  }
+  return gemm_impl(A, b->slot[b->rank][slot], C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream, nullptr,
+                   nullptr, 1, &h);
 }
 
 extern "C" B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,

@@ -173,7 +173,39 @@ struct GemmParams {
   uint64_t* flags;       // [split tiles][sk_parts-1][2 CTAs]
   EpilogueParams epi;
   int32_t num_out;       // output tensor maps each C tile is stored to (1, or one per rank when gathering)
+  // Exchange hooks (pair kernel, b200_bcast_gemm): B is a receive slot that
+  // other GPUs fill.  Every producer waits until each dep flag has reached
+  // dep_value before its first load; once all of the grid's loads have
+  // landed, the last CTA pair writes rel_value into every rel flag (the
+  // writers' "slot free" flags, in their memory) and resets rel_counter.
+  const uint32_t* dep_flags[8];
+  uint32_t* rel_flags[8];
+  uint32_t* rel_counter;
+  int32_t n_dep, n_rel;
+  uint32_t dep_value, rel_value;
 };
+
+// Exchange hooks of GemmParams: producer side.  Returns false when a flag
+// did not arrive in time.
+__device__ __forceinline__ bool wait_deps(const GemmParams& p) {
+  for (int i = 0; i < p.n_dep; ++i) {
+    if (!wait_flag_reached(p.dep_flags[i], p.dep_value, p.timeout_ns)) return false;
+  }
+  fence_proxy_async_global();  // the flags' acquire comes before this thread's TMA reads of B
+  return true;
+}
+// Called once per CTA pair (its leader's producer) after every load of the
+// pair has landed, also on an error path (the writers must not wait for a
+// release that never comes).  The last pair to finish releases the slot.
+__device__ __forceinline__ void release_slot(const GemmParams& p, int num_pairs) {
+  if (p.rel_counter == nullptr) return;
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.rel_counter) : "memory");
+  if (old + 1u == (uint32_t)num_pairs) {
+    for (int i = 0; i < p.n_rel; ++i) st_release_sys_u32(p.rel_flags[i], p.rel_value);
+    asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(p.rel_counter) : "memory");
+  }
+}
 
 // Output tensor maps of the gathering GEMM (b200_gemm_bf16_allgather): the
 // rows this rank computes, in every rank's gathered C, each mapped in this

@@ -166,6 +166,11 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
+      // B filled by other GPUs (exchange hooks): its flags before any load.
+      if (p.n_dep > 0 && !wait_deps(p)) {
+        raise_status(p, abort_flag, kDevTimeoutPeer);
+        ok = false;
+      }
       for (int w = pair; w < p.num_work && ok; w += num_pairs) {
         const WorkItem wk = work_item(w, p);
         const int row0 = wk.mb * kPairBM + (int)rank * kBM;
@@ -212,6 +217,8 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
             break;
           }
         }
+        // Every load of this pair has landed: B's slot is no longer read here.
+        release_slot(p, num_pairs);
       }
     }
     __syncwarp();

@@ -1,0 +1,35 @@
+// Internal layout of b200_bcast (include/b200_gemm.h), shared by the
+// exchange protocol (peer_copy.cu) and the GEMM that waits for and releases
+// the exchange's slots inside the kernel (b200_gemm.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace b200 {
+constexpr int kBcastSlots = 2;
+constexpr int kBcastMaxWorld = 8;
+}  // namespace b200
+
+struct b200_bcast {
+  int rank, world;
+  size_t nbytes;
+  char* slot[b200::kBcastMaxWorld][b200::kBcastSlots];  // every rank's slots as mapped in this process
+  char* flags[b200::kBcastMaxWorld];                    // every rank's flag array as mapped in this process
+};
+
+namespace b200 {
+// Flag array of one rank (uint32): ready[slot][sender], done[rank], then one
+// counter private to that rank (the in-kernel release's count of finished
+// CTA pairs).
+inline uint32_t* bcast_ready(const b200_bcast* b, int owner, int slot, int sender) {
+  return reinterpret_cast<uint32_t*>(b->flags[owner]) + slot * b->world + sender;
+}
+inline uint32_t* bcast_done(const b200_bcast* b, int owner, int r) {
+  return reinterpret_cast<uint32_t*>(b->flags[owner]) + kBcastSlots * b->world + r;
+}
+inline uint32_t* bcast_counter(const b200_bcast* b) {
+  return reinterpret_cast<uint32_t*>(b->flags[b->rank]) + kBcastSlots * b->world + b->world;
+}
+inline size_t bcast_flag_words(int world) { return (size_t)(kBcastSlots * world + world + 1); }
+}  // namespace b200

@@ -22,6 +22,7 @@
 #include <new>
 
 #include "b200_gemm.h"
+#include "peer_bcast.h"
 
 namespace {
 
@@ -96,24 +97,12 @@ extern "C" B200_API int b200_wait_u32(const void* flag, uint32_t value, void* st
 // until that peer is done with step s - kSlots, which used the same slot.
 // ---------------------------------------------------------------------------
 namespace {
-constexpr int kBcastSlots = 2;
-constexpr int kBcastMaxWorld = 8;
-}  // namespace
-
-struct b200_bcast {
-  int rank, world;
-  size_t nbytes;
-  char* slot[kBcastMaxWorld][kBcastSlots];  // every rank's slots as mapped in this process
-  char* flags[kBcastMaxWorld];              // every rank's flag array as mapped in this process
-};
-
-namespace {
+using b200::kBcastMaxWorld;
+using b200::kBcastSlots;
 inline uint32_t* ready_flag(const b200_bcast* b, int owner, int slot, int sender) {
-  return reinterpret_cast<uint32_t*>(b->flags[owner]) + slot * b->world + sender;
+  return b200::bcast_ready(b, owner, slot, sender);
 }
-inline uint32_t* done_flag(const b200_bcast* b, int owner, int r) {
-  return reinterpret_cast<uint32_t*>(b->flags[owner]) + kBcastSlots * b->world + r;
-}
+inline uint32_t* done_flag(const b200_bcast* b, int owner, int r) { return b200::bcast_done(b, owner, r); }
 }  // namespace
 
 extern "C" B200_API int b200_bcast_piece(int world, size_t nbytes, int index, size_t* offset, size_t* length) {
@@ -130,9 +119,7 @@ extern "C" B200_API int b200_bcast_piece(int world, size_t nbytes, int index, si
   return B200_OK;
 }
 
-extern "C" B200_API size_t b200_bcast_flag_bytes(int world) {
-  return (size_t)(kBcastSlots * world + world) * sizeof(uint32_t);
-}
+extern "C" B200_API size_t b200_bcast_flag_bytes(int world) { return b200::bcast_flag_words(world) * sizeof(uint32_t); }
 
 extern "C" B200_API int b200_bcast_create(int rank, int world, size_t nbytes, void* const* slots, void* const* flags,
                                           b200_bcast** out) {

@@ -27,6 +27,7 @@ enum DeviceStatus : uint32_t {
   kDevTimeoutDrain = 8u,      // teardown gave up waiting for in-flight copies
   kDevWrongArch = 16u,        // a copy of the kernel built without sm_100a features ran
   kDevTimeoutSplitK = 32u,    // the last split-K part gave up waiting for a partial
+  kDevTimeoutPeer = 64u,      // the producer gave up waiting for another GPU's data (exchange flags)
 };
 
 // Kernel bodies use tcgen05/TMA, which exist only in the sm_100a feature set.
@@ -151,6 +152,35 @@ __device__ __forceinline__ bool wait_flag_eq(const uint64_t* flag, uint64_t valu
     if (globaltimer_ns() - t0 > timeout_ns) return false;
   }
 }
+// Flags written by another GPU (copy-engine exchange, b200_bcast_*): 32-bit
+// step counters compared wrap-aware, read with acquire at system scope.
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until (int32_t)(*flag - value) >= 0; false after timeout_ns.
+__device__ __forceinline__ bool wait_flag_reached(const uint32_t* flag, uint32_t value, uint64_t timeout_ns) {
+  if ((int32_t)(ld_acquire_sys_u32(flag) - value) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if ((int32_t)(ld_acquire_sys_u32(flag) - value) >= 0) return true;
+      __nanosleep(128);
+    }
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+// Orders this thread's earlier generic-proxy accesses (e.g. the acquire of a
+// flag) before its later async-proxy global accesses (TMA loads).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Named barrier for a subset of the CTA's warps (id != 0).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -183,6 +183,23 @@ B200_API int b200_bcast_release(b200_bcast* b, int64_t step, void* stream);
 B200_API void b200_bcast_destroy(b200_bcast* b);
 
 /*
+ * The GEMM of exchange step `step` on this rank: C = A * op(B) with B this
+ * rank's receive slot of that step (rank 0: B0, its own source buffer), in
+ * the layout rank 0 sent (ldb as for b200_gemm_bf16).  In place of
+ * b200_bcast_wait before and b200_bcast_release after: on the CTA-pair
+ * kernel the producer waits for the step's flags itself (bounded: a flag
+ * that does not arrive within the wait limit is reported by
+ * b200_gemm_status) and the last CTA pair to finish loading B releases the
+ * slot, so nothing stands between consecutive launches on `stream` and they
+ * keep their programmatic overlap; the other kernels get the stream
+ * operations around their launch.  Calls on one rank go on one stream.
+ * No reference counterpart.
+ */
+B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, const void* A, const void* B0, void* C, int64_t M,
+                             int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout,
+                             void* stream);
+
+/*
  * FP32 GEMM, the reference's fp32_matmul operator (fp32_matmul/matmul.cpp:3-9,
  * MatmulFn over float; B stored [K,N] row-major there, B200_B_KN here; [N,K]
  * also accepted): C[M,N] fp32 = A[M,K] fp32 x op(B) fp32, computed on the bf16

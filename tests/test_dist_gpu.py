@@ -141,19 +141,28 @@ def _peer_bcast_worker(rank, world, port, nbytes, steps, result_dir):
         srcs = [payload(s) for s in range(steps + 1)] if rank == 0 else None
         pb.issue(0, srcs[0] if rank == 0 else None)
         ok = True
-        K = N = 256
+        K, N = 256, 1024  # B [K, N] read from the front of each step's buffer
         for s in range(steps):
             pb.issue(s + 1, srcs[s + 1] if rank == 0 else None)
-            pb.wait(s, stream)
-            got = pb.data(s, srcs[s] if rank == 0 else None)
-            ok &= bool(torch.equal(got, payload(s)))  # on `stream`, after the wait
-            # a GEMM reading the delivered bytes as B [K, N] (the bench's use)
-            a = torch.ones((64, K), dtype=torch.bfloat16, device=dev)
-            bmat = got[:K * N * 2].view(torch.bfloat16).view(K, N)
-            c = b200_gemm.gemm(a, bmat, b_layout="kn")
-            ref = b200_gemm.gemm(a, payload(s)[:K * N * 2].view(torch.bfloat16).view(K, N), b_layout="kn")
+            ref_b = payload(s)[:K * N * 2].view(torch.bfloat16).view(K, N)
+            src_b = srcs[s][:K * N * 2].view(torch.bfloat16).view(K, N) if rank == 0 else None
+            if s % 3 == 0:
+                # explicit wait / read / release
+                pb.wait(s, stream)
+                got = pb.data(s, srcs[s] if rank == 0 else None)
+                ok &= bool(torch.equal(got, payload(s)))  # on `stream`, after the wait
+                a = torch.ones((64, K), dtype=torch.bfloat16, device=dev)
+                c = b200_gemm.gemm(a, got[:K * N * 2].view(torch.bfloat16).view(K, N), b_layout="kn")
+                pb.release(s, stream)
+            else:
+                # the GEMM waits and releases itself: M = 2048 takes the CTA-pair
+                # kernel (in-kernel flags), M = 64 the skinny kernel (stream operations)
+                m = 2048 if s % 3 == 1 else 64
+                a = torch.ones((m, K), dtype=torch.bfloat16, device=dev)
+                c = torch.empty((m, N), dtype=torch.bfloat16, device=dev)
+                pb.gemm(s, a, (K, N), out=c, b_layout="kn", src=src_b, stream=stream)
+            ref = b200_gemm.gemm(a, ref_b, b_layout="kn")
             ok &= bool(torch.equal(torch.nan_to_num(c, nan=0.0), torch.nan_to_num(ref, nan=0.0)))
-            pb.release(s, stream)
         torch.cuda.synchronize()
         pb.close()
         assert b200_gemm.check_status() == 0
@@ -169,8 +178,9 @@ def _peer_bcast_worker(rank, world, port, nbytes, steps, result_dir):
 def test_peer_broadcast_delivers_every_step(tmp_path, nbytes):
     """PeerBroadcast (copy engines + stream-ordered flags): over several steps,
     with two receive slots reused in turn, every rank receives exactly the
-    bytes rank 0 sent for that step, and a GEMM reading them on the same
-    stream sees them."""
+    bytes rank 0 sent for that step, and a GEMM reading them sees them — after
+    an explicit wait, and through b200_bcast_gemm, which waits and releases
+    inside the CTA-pair kernel or with stream operations around the others."""
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs at least 2 GPUs")
