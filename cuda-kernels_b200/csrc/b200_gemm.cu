@@ -54,20 +54,17 @@ constexpr int kPairWideStages = 4;
 constexpr int kGroupM = 16;
 
 // Skinny (M <= 128) configurations: UMMA N = MPAD, ring depth per MPAD.
-// For MPAD <= 64 the ring is kept small enough (<= 100 KiB with the
-// reduction scratch inside it) that two CTAs fit on an SM: in a chain of
-// launches the next GEMM's CTAs become resident while this one runs and
-// prefetch their weights into L2 before the launch wait, so one GEMM's
-// epilogue overlaps the next one's weight stream.  4-5 stages of 16 KiB of
-// weights still keep ~80 KiB in flight per SM, enough for HBM rate.
+// (Measured on B200: rings of 4-5 stages, small enough for two CTAs per SM
+// so that the next launch's CTAs could prefetch its weights while this one
+// runs, were 10-20 % slower in back-to-back launches.)
 template <int MPAD>
 struct SkinnyCfg;
 template <>
-struct SkinnyCfg<16> { static constexpr int kStages = 5; };
+struct SkinnyCfg<16> { static constexpr int kStages = 10; };
 template <>
-struct SkinnyCfg<32> { static constexpr int kStages = 5; };
+struct SkinnyCfg<32> { static constexpr int kStages = 9; };
 template <>
-struct SkinnyCfg<64> { static constexpr int kStages = 4; };
+struct SkinnyCfg<64> { static constexpr int kStages = 8; };
 template <>
 struct SkinnyCfg<128> { static constexpr int kStages = 6; };
 constexpr int kMaxClusterSplits = 8;  // portable cluster size limit

@@ -182,10 +182,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // of HBM (for these short, HBM-bound launches the first-load latency is a
   // large part of the fixed cost).
   if (warp == 0 && lane == 0) {
-    // Up to 16 K-blocks (256 KiB of weights per CTA): with two CTAs per SM
-    // this launch's CTAs can be resident long before the previous kernel
-    // ends, and the whole weight slice of a 4096-wide problem is then in L2.
-    const int npf = min(my_kb, max(STAGES, 16));
+    const int npf = min(my_kb, STAGES);
     for (int i = 0; i < npf; ++i) {
       const int kb = kb_begin + i;
       if constexpr (!B_MN) {
