@@ -85,6 +85,9 @@ struct DeviceState {
   // shares add up to exactly the pool of a launch at kAttnRegsLaunch
   // registers per thread, so it only runs when the binary has that count.
   bool attn_regs_ok = false;
+  // Same for the eight-epilogue-warp wide pair kernel (kWide8Regs*); when the
+  // binary has another count, the four-warp wide kernel is used instead.
+  bool wide8_regs_ok = false;
 };
 
 // Split-K plan for the pair kernel's last, partial wave of tiles (see
@@ -211,6 +214,18 @@ int init_device(int dev, DeviceState& st) {
     cudaFuncAttributes fa{};
     if (cudaFuncGetAttributes(&fa, b200::flash_attn_fwd_kernel) != cudaSuccess) return B200_ERR_CUDA;
     st.attn_regs_ok = fa.numRegs == (int)b200::kAttnRegsLaunch;
+  }
+  {
+    st.wide8_regs_ok = true;
+    const void* w8[2] = {(const void*)b200::gemm_bf16_pair_wide8_kernel<false>,
+                         (const void*)b200::gemm_bf16_pair_wide8_kernel<true>};
+    for (const void* k : w8) {
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem) != cudaSuccess)
+        return B200_ERR_CUDA;
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return B200_ERR_CUDA;
+      if (fa.numRegs != (int)b200::kWide8RegsLaunch) st.wide8_regs_ok = false;
+    }
   }
   if (set_skinny_attrs<16>() != B200_OK || set_skinny_attrs<32>() != B200_OK || set_skinny_attrs<64>() != B200_OK ||
       set_skinny_attrs<128>() != B200_OK)
@@ -657,7 +672,13 @@ int gemm_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
                      : cudaLaunchKernelEx(&cfg, b200::gemm_bf16_pair_gather_kernel<false>, tmA, tmB, *outs, p);
     return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
-  const PairKernel kern = kPair[use_wide ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
+  PairKernel kern = kPair[use_wide ? 1 : 0][p.b_mn_major ? 1 : 0][fused ? 1 : 0];
+  if (use_wide && !fused && st->wide8_regs_ok) {
+    // Plain 256 x 512 tiles: eight epilogue warps free the accumulator from
+    // registers (gemm_sm100_pair.cuh, kWide8Threads).
+    kern = p.b_mn_major ? b200::gemm_bf16_pair_wide8_kernel<true> : b200::gemm_bf16_pair_wide8_kernel<false>;
+    cfg.blockDim = dim3(b200::kWide8Threads, 1, 1);
+  }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
@@ -683,7 +704,7 @@ extern "C" B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, const void*
   PeerHooks h{};
   for (int r = 0; r < b->world; ++r) {
     if (r == b->rank) continue;
-    h.dep[h.n_dep++] = b200::bcast_ready(b, b->rank, slot, r);  // every piece of this step's slot has landed
+    h.dep[h.n_dep++] = b200::bcast_ready(b, b->rank, slot, r, b200::kBcastParts - 1);  // r's copies have landed
     h.rel[h.n_rel++] = b200::bcast_done(b, r, b->rank);        // each writer: this rank is done with the slot
   }
   h.counter = b200::bcast_counter(b);

@@ -35,6 +35,21 @@ namespace b200 {
 
 constexpr int kPairBM = 256;  // rows of C per pair tile (128 per CTA)
 
+// The 256 x 512 tile with eight epilogue warps (384 threads): warps 0-3 hold
+// the producer and the MMA issuer and give registers away, warps 4-11 drain
+// the accumulator, two per TMEM lane quarter, one per 256-column half.  Each
+// epilogue thread pulls its row's 256 columns out of TMEM into 128 registers
+// of packed bf16 and frees its half of the accumulator at once; the C stores
+// then leave from registers while the next tile's MMAs already run (with
+// four epilogue warps the next tile waited for the stores: all CTAs drain at
+// the same moment and the stores are slow).  Register shares: 128 threads x
+// 56 + 256 x 224 = 384 x 168, the pool of a launch at 168 registers; the
+// host uses this kernel only when the binary has that count.
+constexpr int kWide8Threads = 384;
+constexpr uint32_t kWide8RegsLaunch = 168, kWide8RegsOther = 56, kWide8RegsEpi = 224;
+static_assert(128 * kWide8RegsOther + 256 * kWide8RegsEpi <= kWide8Threads * kWide8RegsLaunch,
+              "register reallocation exceeds the launch pool");
+
 template <int BN, int STAGES>
 struct PairSmemPlan {
   // A tile of BN columns is computed as kNSub pair MMAs of N = 256 each
@@ -70,13 +85,14 @@ struct PairSmemPlan {
 
 // Kernel body, shared by the plain/fused kernel (one output map) and the
 // gathering kernel (one output map per rank: every C tile is stored to each).
-template <int BN, int STAGES, bool B_MN, bool EPI>
+template <int BN, int STAGES, bool B_MN, bool EPI, int EW = 4>
 __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
                                                const CUtensorMap* outs, const int n_out, const GemmParams& p) {
   using Plan = PairSmemPlan<BN, STAGES>;
   constexpr int kNSub = Plan::kNSub;
   constexpr int kAccN = Plan::kAccN;
   static_assert(BN == 256 || BN == 512, "pair tiles are 256 x 256 or 256 x 512");
+  static_assert(EW == 4 || (EW == 8 && BN == 512 && !EPI), "eight epilogue warps: plain 256 x 512 tiles only");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -155,6 +171,10 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
   pdl_launch_dependents();
   pdl_wait();
 
+  // Warps 0-1 (with eight epilogue warps: the whole first warpgroup, 0-3,
+  // which gives registers to the epilogue warpgroups) produce and issue.
+  if (warp < (EW == 8 ? 4 : 2)) {
+  if constexpr (EW == 8) setmaxnreg_dec<kWide8RegsOther>();
   if (warp == 0) {
     // ---- TMA producer (both CTAs) ---------------------------------------------
     if (lane == 0) {
@@ -294,6 +314,71 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
       if (!mbar_wait(drain_bar, 0u, p.timeout_ns, nullptr)) raise_status(p, abort_flag, kDevTimeoutDrain);
     }
     __syncwarp();
+  }
+  } else if constexpr (EW == 8) {
+    // ---- epilogue, eight warps (4..11 of both CTAs): whole halves into registers ----
+    setmaxnreg_inc<kWide8RegsEpi>();
+    {
+      const int ew = warp - 4;
+      const int q = warp & 3;  // TMEM lane quarter
+      const int h = ew >> 2;   // accumulator half: columns [256 h, 256 h + 256)
+      const uint32_t tmem_lane = (uint32_t)(q * 32) << 16;
+      const uint32_t buf = sC + (uint32_t)(ew * kEpiBufBytes);  // one 4 KiB staging buffer per warp
+      uint32_t acc_phase = 0;
+      for (int w = pair; w < p.num_work; w += num_pairs) {
+        const WorkItem wk = work_item(w, p);
+        const bool got = mbar_wait(accf_bar(0), acc_phase, p.timeout_ns, abort_flag);
+        if (!named_bar_and(2, 8 * 32, got)) {
+          if (lane == 0) raise_status(p, abort_flag, kDevTimeoutEpilogue);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + tmem_lane + (uint32_t)(h * Plan::kMmaN);
+        uint32_t pk[128];  // this row's 256 columns as packed bf16 pairs
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(t_row + c * kEpiCols, r0);
+          tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, r1);
+          tmem_ld_wait_regs(r0);
+          tmem_ld_wait_regs(r1);
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(__uint_as_float(r0[2 * k]), __uint_as_float(r0[2 * k + 1]));
+            __nv_bfloat162 hi = __floats2bfloat162_rn(__uint_as_float(r1[2 * k]), __uint_as_float(r1[2 * k + 1]));
+            pk[c * 32 + k] = *reinterpret_cast<uint32_t*>(&lo);
+            pk[c * 32 + 16 + k] = *reinterpret_cast<uint32_t*>(&hi);
+          }
+        }
+        // This half of the accumulator is in registers: hand it back now.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(acce_bar(0, h), 0));
+        const int row = wk.mb * kPairBM + (int)rank * kBM + q * kEpiRowsPerWarp;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read `buf`
+          __syncwarp();
+          const uint32_t row_addr = buf + lane * 128u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t dst = row_addr + (((uint32_t)j ^ (lane & 7u)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(pk[c * 32 + 4 * j]),
+                         "r"(pk[c * 32 + 4 * j + 1]), "r"(pk[c * 32 + 4 * j + 2]), "r"(pk[c * 32 + 4 * j + 3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(outs, buf, wk.nb * BN + h * Plan::kMmaN + c * kEpiCols, row);
+            bulk_commit_group();
+          }
+        }
+        acc_phase ^= 1u;
+      }
+      if (lane == 0) bulk_wait_group_read<0>();  // smem reads done; the global writes complete with the grid
+      __syncwarp();
+    }
   } else {
     // ---- epilogue (warps 2..5 of both CTAs) ------------------------------------------
     const int q = warp & 3;
@@ -449,6 +534,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
 #else
   pair_gemm_body<BN, STAGES, B_MN, EPI>(tmA, tmB, &tmC, 1, p);
+#endif
+}
+
+// 256 x 512 tiles, plain epilogue, eight epilogue warps (see kWide8Threads).
+template <bool B_MN>
+__global__ void __launch_bounds__(kWide8Threads, 1)
+    gemm_bf16_pair_wide8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ GemmParams p) {
+#if B200_NO_SM100A_FEATURES
+  if (threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, (uint32_t)kDevWrongArch);
+#else
+  pair_gemm_body<512, 4, B_MN, false, 8>(tmA, tmB, &tmC, 1, p);
 #endif
 }
 

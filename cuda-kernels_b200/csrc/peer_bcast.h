@@ -9,6 +9,10 @@
 namespace b200 {
 constexpr int kBcastSlots = 2;
 constexpr int kBcastMaxWorld = 8;
+// Each piece moves in this many parts: part k of every piece leaves rank 0
+// before part k + 1 of any, and a receiving rank forwards a part as soon as
+// it has landed, so forwarding overlaps rank 0's sending.
+constexpr int kBcastParts = 4;
 }  // namespace b200
 
 struct b200_bcast {
@@ -19,17 +23,18 @@ struct b200_bcast {
 };
 
 namespace b200 {
-// Flag array of one rank (uint32): ready[slot][sender], done[rank], then one
-// counter private to that rank (the in-kernel release's count of finished
-// CTA pairs).
-inline uint32_t* bcast_ready(const b200_bcast* b, int owner, int slot, int sender) {
-  return reinterpret_cast<uint32_t*>(b->flags[owner]) + slot * b->world + sender;
+// Flag array of one rank (uint32): ready[slot][sender][part], done[rank],
+// then one counter private to that rank (the in-kernel release's count of
+// finished CTA pairs).  A sender's copies into a slot run in order on one
+// stream, so ready[slot][sender][last part] means all of them have landed.
+inline uint32_t* bcast_ready(const b200_bcast* b, int owner, int slot, int sender, int part) {
+  return reinterpret_cast<uint32_t*>(b->flags[owner]) + (slot * b->world + sender) * kBcastParts + part;
 }
 inline uint32_t* bcast_done(const b200_bcast* b, int owner, int r) {
-  return reinterpret_cast<uint32_t*>(b->flags[owner]) + kBcastSlots * b->world + r;
+  return reinterpret_cast<uint32_t*>(b->flags[owner]) + kBcastSlots * b->world * kBcastParts + r;
 }
 inline uint32_t* bcast_counter(const b200_bcast* b) {
-  return reinterpret_cast<uint32_t*>(b->flags[b->rank]) + kBcastSlots * b->world + b->world;
+  return reinterpret_cast<uint32_t*>(b->flags[b->rank]) + kBcastSlots * b->world * kBcastParts + b->world;
 }
-inline size_t bcast_flag_words(int world) { return (size_t)(kBcastSlots * world + world + 1); }
+inline size_t bcast_flag_words(int world) { return (size_t)(kBcastSlots * world * kBcastParts + world + 1); }
 }  // namespace b200

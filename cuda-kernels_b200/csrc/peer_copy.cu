@@ -88,21 +88,33 @@ extern "C" B200_API int b200_wait_u32(const void* flag, uint32_t value, void* st
 //
 // Every rank owns kSlots receive slots of `nbytes` (step s uses slot
 // s % kSlots) and a flag array, all mapped by every peer (CUDA IPC).  Flags
-// (uint32): ready[slot][sender] — the sender's piece of that slot has landed
-// (value step + 1); done[rank] — that rank has finished reading its slot of
-// a step (value step + 1).  Pieces: the buffer is cut into world - 1 pieces
-// (b200_bcast_piece); rank 0 sends piece q-1 to rank q, and rank q forwards
-// it to every other receiving rank once it has landed, so every byte leaves
-// rank 0 once.  Before writing into a peer's slot for step s, a writer waits
+// (uint32): ready[slot][sender][part] — that part of the sender's piece of
+// that slot has landed (value step + 1); done[rank] — that rank has finished
+// reading its slot of a step (value step + 1).  Pieces: the buffer is cut
+// into world - 1 pieces (b200_bcast_piece), each moved in kBcastParts parts;
+// rank 0 sends piece q-1 to rank q, part by part across all pieces, and rank
+// q forwards each part to every other receiving rank as soon as it has
+// landed, so every byte leaves rank 0 once and forwarding overlaps sending.  Before writing into a peer's slot for step s, a writer waits
 // until that peer is done with step s - kSlots, which used the same slot.
 // ---------------------------------------------------------------------------
 namespace {
 using b200::kBcastMaxWorld;
+using b200::kBcastParts;
 using b200::kBcastSlots;
-inline uint32_t* ready_flag(const b200_bcast* b, int owner, int slot, int sender) {
-  return b200::bcast_ready(b, owner, slot, sender);
+inline uint32_t* ready_flag(const b200_bcast* b, int owner, int slot, int sender, int part) {
+  return b200::bcast_ready(b, owner, slot, sender, part);
 }
 inline uint32_t* done_flag(const b200_bcast* b, int owner, int r) { return b200::bcast_done(b, owner, r); }
+// Part k of a piece [off, off + len): 256-byte aligned starts.
+inline void piece_part(size_t off, size_t len, int k, size_t* poff, size_t* plen) {
+  auto bound = [&](int i) -> size_t {
+    if (i >= kBcastParts) return off + len;
+    size_t x = off + (len * (size_t)i / kBcastParts + 255) / 256 * 256;
+    return x < off + len ? x : off + len;
+  };
+  *poff = bound(k);
+  *plen = bound(k + 1) - *poff;
+}
 }  // namespace
 
 extern "C" B200_API int b200_bcast_piece(int world, size_t nbytes, int index, size_t* offset, size_t* length) {
@@ -155,24 +167,36 @@ extern "C" B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void
   int rc;
   if (b->rank == 0) {
     if (src == nullptr) return B200_ERR_INVALID_ARG;
-    for (int q = 1; q < b->world; ++q) {
-      size_t off, len;
-      if ((rc = b200_bcast_piece(b->world, b->nbytes, q - 1, &off, &len)) != B200_OK) return rc;
-      if (reuse && (rc = b200_wait_u32(done_flag(b, 0, q), v_prev, stream)) != B200_OK) return rc;
-      if ((rc = b200_copy_async(b->slot[q][slot] + off, static_cast<const char*>(src) + off, len, stream)) != B200_OK)
-        return rc;
-      if ((rc = b200_signal_u32(ready_flag(b, q, slot, 0), v, stream)) != B200_OK) return rc;
+    // part k of every piece, then part k + 1: every receiver can start
+    // forwarding after the first round
+    for (int k = 0; k < kBcastParts; ++k) {
+      for (int q = 1; q < b->world; ++q) {
+        size_t off, len, poff, plen;
+        if ((rc = b200_bcast_piece(b->world, b->nbytes, q - 1, &off, &len)) != B200_OK) return rc;
+        piece_part(off, len, k, &poff, &plen);
+        if (k == 0 && reuse && (rc = b200_wait_u32(done_flag(b, 0, q), v_prev, stream)) != B200_OK) return rc;
+        if ((rc = b200_copy_async(b->slot[q][slot] + poff, static_cast<const char*>(src) + poff, plen, stream)) !=
+            B200_OK)
+          return rc;
+        if ((rc = b200_signal_u32(ready_flag(b, q, slot, 0, k), v, stream)) != B200_OK) return rc;
+      }
     }
     return B200_OK;
   }
   size_t off, len;
   if ((rc = b200_bcast_piece(b->world, b->nbytes, b->rank - 1, &off, &len)) != B200_OK) return rc;
-  if ((rc = b200_wait_u32(ready_flag(b, b->rank, slot, 0), v, stream)) != B200_OK) return rc;  // my piece is here
-  for (int r = 1; r < b->world; ++r) {
-    if (r == b->rank) continue;
-    if (reuse && (rc = b200_wait_u32(done_flag(b, b->rank, r), v_prev, stream)) != B200_OK) return rc;
-    if ((rc = b200_copy_async(b->slot[r][slot] + off, b->slot[b->rank][slot] + off, len, stream)) != B200_OK) return rc;
-    if ((rc = b200_signal_u32(ready_flag(b, r, slot, b->rank), v, stream)) != B200_OK) return rc;
+  for (int k = 0; k < kBcastParts; ++k) {
+    size_t poff, plen;
+    piece_part(off, len, k, &poff, &plen);
+    // part k of my piece has landed: pass it on
+    if ((rc = b200_wait_u32(ready_flag(b, b->rank, slot, 0, k), v, stream)) != B200_OK) return rc;
+    for (int r = 1; r < b->world; ++r) {
+      if (r == b->rank) continue;
+      if (k == 0 && reuse && (rc = b200_wait_u32(done_flag(b, b->rank, r), v_prev, stream)) != B200_OK) return rc;
+      if ((rc = b200_copy_async(b->slot[r][slot] + poff, b->slot[b->rank][slot] + poff, plen, stream)) != B200_OK)
+        return rc;
+      if ((rc = b200_signal_u32(ready_flag(b, r, slot, b->rank, k), v, stream)) != B200_OK) return rc;
+    }
   }
   return B200_OK;
 }
@@ -183,7 +207,7 @@ extern "C" B200_API int b200_bcast_wait(b200_bcast* b, int64_t step, void* strea
   const int slot = (int)(step % kBcastSlots);
   for (int r = 0; r < b->world; ++r) {
     if (r == b->rank) continue;
-    const int rc = b200_wait_u32(ready_flag(b, b->rank, slot, r), (uint32_t)(step + 1), stream);
+    const int rc = b200_wait_u32(ready_flag(b, b->rank, slot, r, kBcastParts - 1), (uint32_t)(step + 1), stream);
     if (rc != B200_OK) return rc;
   }
   return B200_OK;
