@@ -1067,20 +1067,24 @@ def _multi_gpu_parity(a, b, layout, world, rank, b200_gemm):
 
 def _rowshard_object(args, world, rank, dev, b200_gemm):
     """BASELINE config 5 at this N: C = A B with A [131072, 8192] split into one
-    row panel per rank, B [8192, 8192] broadcast from rank 0, C sharded.
-    gemm_only_ms: the panel GEMMs alone; broadcast_plus_gemm_ms: B broadcast
-    (NCCL) then the GEMM, per step; both device-timed, max over ranks.  At N>1
-    rank 0 also runs the whole job alone (the N=1 figure in the same run), so
-    the speed-up is measured, not assumed."""
+    row panel per rank, B [8192, 8192] (stored [N, K], the reference's layout)
+    broadcast from rank 0, C sharded.  gemm_only_ms: the panel GEMMs alone;
+    broadcast_plus_gemm_ms: the whole job, B from rank 0 on the copy engines
+    in two parts (the GEMM of the first 1024 columns of C starts when their
+    rows of B have arrived, the rest of B moves meanwhile,
+    dist.row_sharded_gemm_peer); nccl_broadcast_plus_gemm_ms: the same job with
+    an NCCL broadcast of B before the GEMM; all device-timed, max over ranks.
+    At N>1 rank 0 also runs the whole job alone (the N=1 figure in the same
+    run), so the speed-up is measured, not assumed."""
     import torch
     import torch.distributed as dist
-    from b200_gemm.dist import row_sharded_gemm, shard_rows
+    from b200_gemm.dist import PeerBroadcast, row_sharded_gemm, row_sharded_gemm_peer, shard_rows
     Mt, N, K = args.rowshard_m, 8192, 8192
     flops = 2.0 * Mt * N * K
     s, e = shard_rows(Mt, world, rank)
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     a = (torch.rand((e - s, K), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
-    b = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)
+    b = (torch.rand((N, K), generator=g, device=dev) * 2 - 1).to(torch.bfloat16)  # [N, K]
     c = torch.empty((e - s, N), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -1106,14 +1110,28 @@ def _rowshard_object(args, world, rank, dev, b200_gemm):
         _barrier(world)
         return _max_over_ranks(e0.elapsed_time(e1) / n, world), n
 
-    gemm_ms, n1 = timed(lambda: row_sharded_gemm(a, b, M=Mt, b_layout="kn", out=c, broadcast=False))
-    both_ms, n2 = timed(lambda: row_sharded_gemm(a, b, M=Mt, b_layout="kn", out=c, broadcast=world > 1))
+    gemm_ms, n1 = timed(lambda: row_sharded_gemm(a, b, M=Mt, b_layout="nk", out=c, broadcast=False))
+    nccl_ms, n3 = timed(lambda: row_sharded_gemm(a, b, M=Mt, b_layout="nk", out=c, broadcast=world > 1))
+    if world > 1:
+        pb = PeerBroadcast(b.numel() * b.element_size())
+        step = [0]
+
+        def job():
+            row_sharded_gemm_peer(a, b, M=Mt, exchange=pb, step=step[0], out=c, first_rows=1024)
+            step[0] += 2
+        both_ms, n2 = timed(job)
+        torch.cuda.synchronize()
+        pb.close()
+    else:
+        both_ms, n2 = nccl_ms, n3
     b200_gemm.check_status()
     del a, c
-    out = {"workload": f"BASELINE config 5: A[{Mt},{K}] row panels x B[{K},{N}] (row-major), U(-1,1), "
-                       f"B broadcast from rank 0 (NCCL), C sharded; strong scaling",
-           "M": Mt, "N": N, "K": K, "panel_rows": e - s, "steps": [n1, n2],
+    out = {"workload": f"BASELINE config 5: A[{Mt},{K}] row panels x B stored [{N},{K}] (C = A B^T), U(-1,1), "
+                       f"B broadcast from rank 0 (copy engines, two parts overlapped with the GEMM), C sharded; "
+                       f"strong scaling",
+           "M": Mt, "N": N, "K": K, "panel_rows": e - s, "steps": [n1, n2, n3],
            "gemm_only_ms": round(gemm_ms, 4), "broadcast_plus_gemm_ms": round(both_ms, 4),
+           "nccl_broadcast_plus_gemm_ms": round(nccl_ms, 4),
            "gemm_only_tflops": round(flops / gemm_ms / 1e9, 1),
            "tflops": round(flops / both_ms / 1e9, 1), "timing": "device, max over ranks"}
     if world > 1:
@@ -1124,13 +1142,13 @@ def _rowshard_object(args, world, rank, dev, b200_gemm):
             a1 = (torch.rand((Mt, K), generator=ga, device=dev) * 2 - 1).to(torch.bfloat16)
             c1 = torch.empty((Mt, N), dtype=torch.bfloat16, device=dev)
             for _ in range(2):
-                b200_gemm.gemm(a1, b, b_layout="kn", out=c1)
+                b200_gemm.gemm(a1, b, b_layout="nk", out=c1)
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             reps = 10
             e0.record(stream)
             for _ in range(reps):
-                b200_gemm.gemm(a1, b, b_layout="kn", out=c1)
+                b200_gemm.gemm(a1, b, b_layout="nk", out=c1)
             e1.record(stream)
             torch.cuda.synchronize()
             t1[0] = e0.elapsed_time(e1) / reps

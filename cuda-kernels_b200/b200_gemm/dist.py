@@ -330,19 +330,22 @@ class PeerBroadcast:
         if rc != _lib.B200_OK:
             raise _lib.B200GemmError(rc, what)
 
-    def issue(self, step: int, src: torch.Tensor | None = None) -> None:
+    def issue(self, step: int, src: torch.Tensor | None = None, offset: int = 0, length: int | None = None) -> None:
         """Queue the copies of step `step` on the copy stream (rank 0: from `src`,
-        a contiguous tensor of nbytes on this device; others: forwarding)."""
+        a contiguous tensor of nbytes on this device; others: forwarding).  With
+        offset / length only those bytes move (offset a multiple of 256), to the
+        same offsets of the step's slot."""
         import ctypes
         if self.world == 1:
             return
+        length = self.nbytes - offset if length is None else length
         ptr = None
         if self.rank == 0:
             if src is None or not src.is_contiguous() or src.numel() * src.element_size() != self.nbytes:
                 raise ValueError("rank 0 needs a contiguous source tensor of nbytes")
             ptr = src.data_ptr()
-        self._check(self._lib.b200_bcast_issue(self._h, step, ctypes.c_void_p(ptr),
-                                               ctypes.c_void_p(self.comm.cuda_stream)), "b200_bcast_issue")
+        self._check(self._lib.b200_bcast_issue_range(self._h, step, ctypes.c_void_p(ptr), offset, length,
+                                                     ctypes.c_void_p(self.comm.cuda_stream)), "b200_bcast_issue")
         if self.rank == 0:
             self._copied[step % self.SLOTS].record(self.comm)
 
@@ -366,12 +369,13 @@ class PeerBroadcast:
                     "b200_bcast_release")
 
     def gemm(self, step: int, a: torch.Tensor, b_shape, *, out: torch.Tensor, b_layout: str = "kn",
-             src: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+             src: torch.Tensor | None = None, stream=None, b_offset: int = 0, ldb: int | None = None) -> torch.Tensor:
         """out = a @ op(B of step `step`) through b200_bcast_gemm, in place of
         wait / gemm / release: the CTA-pair kernel waits for the step's data and
         releases the slot itself, so consecutive GEMMs on `stream` keep their
-        programmatic overlap.  b_shape is B's shape as rank 0 holds it (rank 0
-        passes its B as `src`)."""
+        programmatic overlap.  b_shape is the shape of the B this GEMM reads,
+        starting at byte b_offset of the step's buffer with row pitch ldb
+        (default: b_shape's columns); rank 0 passes that B as `src`."""
         import ctypes
         from . import _lib
         stream = stream if stream is not None else torch.cuda.current_stream(self.device)
@@ -383,8 +387,9 @@ class PeerBroadcast:
         if a.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or a.stride(1) != 1 or out.stride(1) != 1:
             raise ValueError("A and out must be row-major bf16")
         b0 = src.data_ptr() if (self.rank == 0 and src is not None) else None
-        rc = self._lib.b200_bcast_gemm(self._h, step, ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b0),
-                                       ctypes.c_void_p(out.data_ptr()), M, N, K, max(a.stride(0), 1), cols,
+        ldb = cols if ldb is None else ldb
+        rc = self._lib.b200_bcast_gemm(self._h, step, b_offset, ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b0),
+                                       ctypes.c_void_p(out.data_ptr()), M, N, K, max(a.stride(0), 1), ldb,
                                        max(out.stride(0), 1), _lib.B200_B_NK if b_layout == "nk" else _lib.B200_B_KN,
                                        ctypes.c_void_p(stream.cuda_stream))
         self._check(rc, f"b200_bcast_gemm step {step}")
@@ -411,6 +416,51 @@ class PeerBroadcast:
             for p in self._own:
                 self._lib.b200_ipc_free(p)
         self._own = None
+
+
+def row_sharded_gemm_peer(a_local: torch.Tensor, b: torch.Tensor, *, M: int, exchange: "PeerBroadcast", step: int,
+                          out: torch.Tensor | None = None, first_rows: int | None = None,
+                          stream=None) -> ShardedResult:
+    """One row-sharded GEMM job with B (stored [N, K], the reference's layout:
+    its rows are columns of C and contiguous) moved from rank 0 on the copy
+    engines (`exchange`, a PeerBroadcast of B's bytes) in two parts: the first
+    `first_rows` rows as exchange step `step`, the rest as step `step + 1`.
+    The GEMM of the first column block of C starts as soon as its rows have
+    arrived, and the rest of B moves while it runs; each GEMM waits for its
+    rows and releases them inside the kernel (b200_bcast_gemm).  Uses exchange
+    steps `step` and `step + 1`.  On rank 0, `b` is the source."""
+    world = dist.get_world_size()
+    rank = dist.get_rank()
+    start, stop = shard_rows(M, world, rank)
+    if a_local.shape[0] != stop - start:
+        raise ValueError(f"rank {rank}: A panel has {a_local.shape[0]} rows, expected {stop - start}")
+    N, K = b.shape
+    if a_local.shape[1] != K:
+        raise ValueError("inner dimensions of the A panel and B differ")
+    if exchange.nbytes != N * K * b.element_size():
+        raise ValueError("the exchange must be sized for B")
+    if first_rows is None:  # about an eighth of B, whole 256-row blocks
+        first_rows = max(256, (N // 8) // 256 * 256)
+    first_rows = min(first_rows, N)
+    if first_rows % 256 != 0 and first_rows != N:
+        raise ValueError("first_rows must be a multiple of 256")
+    bytes0 = first_rows * K * b.element_size()
+    if out is None:
+        out = torch.empty((stop - start, N), dtype=a_local.dtype, device=a_local.device)
+    src = b if rank == 0 else None
+    exchange.issue(step, src, offset=0, length=bytes0)
+    if first_rows < N:
+        exchange.issue(step + 1, src, offset=bytes0, length=exchange.nbytes - bytes0)
+    exchange.gemm(step, a_local, (first_rows, K), out=out[:, :first_rows], b_layout="nk",
+                  src=b[:first_rows] if rank == 0 else None, stream=stream, b_offset=0, ldb=K)
+    if first_rows < N:
+        exchange.gemm(step + 1, a_local, (N - first_rows, K), out=out[:, first_rows:], b_layout="nk",
+                      src=b[first_rows:] if rank == 0 else None, stream=stream, b_offset=bytes0, ldb=K)
+    else:  # keep the step count of every job at two
+        exchange.issue(step + 1, src, offset=0, length=0)
+        exchange.wait(step + 1, stream if stream is not None else torch.cuda.current_stream(a_local.device))
+        exchange.release(step + 1, stream if stream is not None else torch.cuda.current_stream(a_local.device))
+    return ShardedResult(out, start, stop)
 
 
 def row_sharded_gemm_gather(a_local: torch.Tensor, b: torch.Tensor, *, gathered: GatheredC, M: int,

@@ -690,15 +690,16 @@ extern "C" B200_API int b200_gemm_bf16(const void* A, const void* B, void* C, in
   return gemm_impl(A, B, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
 }
 
-extern "C" B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, const void* A, const void* B0, void* C,
-                                        int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
-                                        int b_layout, void* stream) {
+extern "C" B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, size_t b_offset, const void* A, const void* B0,
+                                        void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                        int64_t ldc, int b_layout, void* stream) {
   if (b == nullptr || step < 0) return B200_ERR_INVALID_ARG;
   if (b->world == 1 || b->rank == 0) return gemm_impl(A, B0, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
   if (M < 0 || N < 0 || K < 0 || b_layout < B200_B_NK || b_layout > B200_B_KN) return B200_ERR_INVALID_ARG;
   const int64_t b_rows = b_layout == B200_B_NK ? N : K;
-  if (b_rows > 0 && ((uint64_t)(b_rows - 1) * (uint64_t)ldb + (uint64_t)(b_layout == B200_B_NK ? K : N)) * 2 >
-                        (uint64_t)b->nbytes)
+  if (b_offset > b->nbytes ||
+      (b_rows > 0 && ((uint64_t)(b_rows - 1) * (uint64_t)ldb + (uint64_t)(b_layout == B200_B_NK ? K : N)) * 2 >
+                         (uint64_t)(b->nbytes - b_offset)))
     return B200_ERR_INVALID_ARG;  // B would run past this rank's slot
   const int slot = (int)(step % b200::kBcastSlots);
   PeerHooks h{};
@@ -712,11 +713,12 @@ extern "C" B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, const void*
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (M == 0 || N == 0 || K == 0) {  // nothing reads B: keep the protocol with stream operations
     int rc = hooks_before(&h, s);
-    if (rc == B200_OK) rc = gemm_impl(A, b->slot[b->rank][slot], C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
+    if (rc == B200_OK)
+      rc = gemm_impl(A, b->slot[b->rank][slot] + b_offset, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream);
     return rc == B200_OK ? hooks_after(&h, s) : rc;
   }
-  return gemm_impl(A, b->slot[b->rank][slot], C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream, nullptr,
-                   nullptr, 1, &h);
+  return gemm_impl(A, b->slot[b->rank][slot] + b_offset, C, M, N, K, lda, ldb, ldc, b_layout, nullptr, 0, stream,
+                   nullptr, nullptr, 1, &h);
 }
 
 extern "C" B200_API int b200_gemm_bf16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,

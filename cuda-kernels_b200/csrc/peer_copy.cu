@@ -158,7 +158,14 @@ extern "C" B200_API int b200_bcast_create(int rank, int world, size_t nbytes, vo
 extern "C" B200_API void b200_bcast_destroy(b200_bcast* b) { delete b; }
 
 extern "C" B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void* src, void* stream) {
+  if (b == nullptr) return B200_ERR_INVALID_ARG;
+  return b200_bcast_issue_range(b, step, src, 0, b->nbytes, stream);
+}
+
+extern "C" B200_API int b200_bcast_issue_range(b200_bcast* b, int64_t step, const void* src, size_t offset,
+                                               size_t length, void* stream) {
   if (b == nullptr || step < 0) return B200_ERR_INVALID_ARG;
+  if (offset > b->nbytes || length > b->nbytes - offset || (offset & 255u) != 0) return B200_ERR_INVALID_ARG;
   if (b->world == 1) return B200_OK;
   const int slot = (int)(step % kBcastSlots);
   const uint32_t v = (uint32_t)(step + 1);
@@ -172,8 +179,8 @@ extern "C" B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void
     for (int k = 0; k < kBcastParts; ++k) {
       for (int q = 1; q < b->world; ++q) {
         size_t off, len, poff, plen;
-        if ((rc = b200_bcast_piece(b->world, b->nbytes, q - 1, &off, &len)) != B200_OK) return rc;
-        piece_part(off, len, k, &poff, &plen);
+        if ((rc = b200_bcast_piece(b->world, length, q - 1, &off, &len)) != B200_OK) return rc;
+        piece_part(offset + off, len, k, &poff, &plen);
         if (k == 0 && reuse && (rc = b200_wait_u32(done_flag(b, 0, q), v_prev, stream)) != B200_OK) return rc;
         if ((rc = b200_copy_async(b->slot[q][slot] + poff, static_cast<const char*>(src) + poff, plen, stream)) !=
             B200_OK)
@@ -184,10 +191,10 @@ extern "C" B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void
     return B200_OK;
   }
   size_t off, len;
-  if ((rc = b200_bcast_piece(b->world, b->nbytes, b->rank - 1, &off, &len)) != B200_OK) return rc;
+  if ((rc = b200_bcast_piece(b->world, length, b->rank - 1, &off, &len)) != B200_OK) return rc;
   for (int k = 0; k < kBcastParts; ++k) {
     size_t poff, plen;
-    piece_part(off, len, k, &poff, &plen);
+    piece_part(offset + off, len, k, &poff, &plen);
     // part k of my piece has landed: pass it on
     if ((rc = b200_wait_u32(ready_flag(b, b->rank, slot, 0, k), v, stream)) != B200_OK) return rc;
     for (int r = 1; r < b->world; ++r) {

@@ -178,14 +178,18 @@ B200_API size_t b200_bcast_flag_bytes(int world);
 B200_API int b200_bcast_create(int rank, int world, size_t nbytes, void* const* slots, void* const* flags,
                                b200_bcast** out);
 B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void* src, void* stream);
+/* The same for bytes [offset, offset + length) of the buffer only (offset a
+   multiple of 256): they land at the same offsets of the step's slot. */
+B200_API int b200_bcast_issue_range(b200_bcast* b, int64_t step, const void* src, size_t offset, size_t length,
+                                    void* stream);
 B200_API int b200_bcast_wait(b200_bcast* b, int64_t step, void* stream);
 B200_API int b200_bcast_release(b200_bcast* b, int64_t step, void* stream);
 B200_API void b200_bcast_destroy(b200_bcast* b);
 
 /*
- * The GEMM of exchange step `step` on this rank: C = A * op(B) with B this
- * rank's receive slot of that step (rank 0: B0, its own source buffer), in
- * the layout rank 0 sent (ldb as for b200_gemm_bf16).  In place of
+ * The GEMM of exchange step `step` on this rank: C = A * op(B) with B at
+ * byte `b_offset` of this rank's receive slot of that step (rank 0: B0, its
+ * own source buffer), in the layout rank 0 sent (ldb as for b200_gemm_bf16).  In place of
  * b200_bcast_wait before and b200_bcast_release after: on the CTA-pair
  * kernel the producer waits for the step's flags itself (bounded: a flag
  * that does not arrive within the wait limit is reported by
@@ -195,8 +199,8 @@ B200_API void b200_bcast_destroy(b200_bcast* b);
  * operations around their launch.  Calls on one rank go on one stream.
  * No reference counterpart.
  */
-B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, const void* A, const void* B0, void* C, int64_t M,
-                             int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout,
+B200_API int b200_bcast_gemm(b200_bcast* b, int64_t step, size_t b_offset, const void* A, const void* B0, void* C,
+                             int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout,
                              void* stream);
 
 /*

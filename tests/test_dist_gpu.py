@@ -187,3 +187,48 @@ def test_peer_broadcast_delivers_every_step(tmp_path, nbytes):
     world = min(world, 8)
     spawn_ranks(_peer_bcast_worker, lambda port: (world, port, nbytes, 7, str(tmp_path)), world)
     assert torch.load(os.path.join(tmp_path, "ok.pt"))
+
+
+def _peer_job_worker(rank, world, port, M, N, K, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+    import torch.distributed as dist
+    import b200_gemm
+    from b200_gemm.dist import PeerBroadcast, row_sharded_gemm, row_sharded_gemm_peer, shard_rows
+    from tests._util import uniform_bf16
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        s, e = shard_rows(M, world, rank)
+        ok = True
+        pb = PeerBroadcast(N * K * 2)
+        for job in range(2):  # two jobs: both slots are reused
+            a = uniform_bf16((M, K), 30 + job)[s:e].cuda()
+            b_full = uniform_bf16((N, K), 40 + job).cuda()
+            b_src = b_full.clone() if rank == 0 else torch.zeros_like(b_full)
+            got = row_sharded_gemm_peer(a, b_src, M=M, exchange=pb, step=2 * job, first_rows=256).c_local
+            ref = row_sharded_gemm(a, b_full, M=M, b_layout="nk", broadcast=False).c_local
+            torch.cuda.synchronize()
+            ok &= bool(torch.equal(got, ref))
+        pb.close()
+        assert b200_gemm.check_status() == 0
+        flag = torch.tensor([int(ok)], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if rank == 0:
+            torch.save(bool(flag.item()), os.path.join(result_dir, "ok.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_job_on_copy_engines(tmp_path):
+    """The row-sharded job with B moved in two parts on the copy engines
+    (dist.row_sharded_gemm_peer: the first block's GEMM waits for its rows and
+    starts while the rest of B moves) gives every rank the same panel of C as
+    the plain GEMM on a local copy of B, bit for bit, over two jobs."""
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(world, 8)
+    spawn_ranks(_peer_job_worker, lambda port: (world, port, 1031 * world, 1280, 520, str(tmp_path)), world)
+    assert torch.load(os.path.join(tmp_path, "ok.pt"))
