@@ -332,25 +332,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   // Launched with programmatic stream serialisation: the prologue above ran
   // while the previous kernel in the stream may still be finishing; wait for
-  // it before loading anything, and let the next kernel start its own
-  // prologue as early as possible.  Before waiting, the producer asks L2 for
-  // the operand tiles of its first tile's first ring's worth of K-blocks (a
-  // prefetch only warms L2, the point of coherence, so it cannot expose data
-  // the previous kernel is still writing).
-  if (warp == 0 && lane == 0 && (int)blockIdx.x < p.num_tiles) {
-    int mb, nb;
-    tile_coords(blockIdx.x, p, mb, nb);
-    const int kb_end = min(p.num_k_blk, STAGES);
-    for (int kb = 0; kb < kb_end; ++kb) {
-      tma_prefetch_l2_2d(&tmA, kb * kBK, mb * kBM);
-      if constexpr (!B_MN) {
-        tma_prefetch_l2_2d(&tmB, kb * kBK, nb * BN);
-      } else {
-#pragma unroll
-        for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, nb * BN + 64 * j, kb * kBK);
-      }
-    }
-  }
+  // it before touching global memory, and let the next kernel start its own
+  // prologue as early as possible.
   pdl_launch_dependents();
   pdl_wait();
 

@@ -144,30 +144,10 @@ __device__ __forceinline__ void pair_gemm_body(const CUtensorMap& tmA, const CUt
   const uint32_t tmem_base = *tmem_holder;
   // Launched with programmatic stream serialisation: the prologue above ran
   // while the previous kernel in the stream may still be finishing; wait for
-  // it before loading anything, and let the next kernel start its own
-  // prologue as early as possible.  Before waiting, the producer asks L2 for
-  // this CTA's operand tiles of its first ring's worth of K-blocks (a
-  // prefetch only warms L2, the point of coherence, so it cannot expose data
-  // the previous kernel is still writing).
-  if (warp == 0 && lane == 0 && pair < p.num_work) {
-    const WorkItem wk = work_item(pair, p);
-    const int row0 = wk.mb * kPairBM + (int)rank * kBM;
-    const int col0 = wk.nb * BN + (int)rank * Plan::kSubCols;
-    const int kb_end = min(wk.kb1, wk.kb0 + STAGES);
-    for (int kb = wk.kb0; kb < kb_end; ++kb) {
-      tma_prefetch_l2_2d(&tmA, kb * kBK, row0);
-#pragma unroll
-      for (int h = 0; h < kNSub; ++h) {
-        const int colh = col0 + h * Plan::kMmaN;
-        if constexpr (!B_MN) {
-          tma_prefetch_l2_2d(&tmB, kb * kBK, colh);
-        } else {
-#pragma unroll
-          for (int j = 0; j < Plan::kSubCols / 64; ++j) tma_prefetch_l2_2d(&tmB, colh + 64 * j, kb * kBK);
-        }
-      }
-    }
-  }
+  // it before touching global memory, and let the next kernel start its own
+  // prologue as early as possible.  (An L2 prefetch of the first operand
+  // tiles before the wait measured neutral here and 6 % slower on the skinny
+  // kernel; there is none.)
   pdl_launch_dependents();
   pdl_wait();
 

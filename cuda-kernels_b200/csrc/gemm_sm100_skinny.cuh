@@ -174,25 +174,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   // Launched with programmatic stream serialisation: the prologue above ran
   // while the previous kernel in the stream may still be finishing; wait for
-  // it before loading anything, and let the next kernel start its own
-  // prologue as early as possible.  Before waiting, ask L2 for the weight
-  // tiles of this CTA's first ring's worth of K-blocks: a prefetch only warms
-  // L2 (the point of coherence), so it is safe while the previous kernel
-  // still runs, and the first loads after the wait then come from L2 instead
-  // of HBM (for these short, HBM-bound launches the first-load latency is a
-  // large part of the fixed cost).
-  if (warp == 0 && lane == 0) {
-    const int npf = min(my_kb, STAGES);
-    for (int i = 0; i < npf; ++i) {
-      const int kb = kb_begin + i;
-      if constexpr (!B_MN) {
-        tma_prefetch_l2_2d(&tmB, kb * kBK, n0);
-      } else {
-        tma_prefetch_l2_2d(&tmB, n0, kb * kBK);
-        tma_prefetch_l2_2d(&tmB, n0 + 64, kb * kBK);
-      }
-    }
-  }
+  // it before touching global memory, and let the next kernel start its own
+  // prologue as early as possible.
   pdl_launch_dependents();
   pdl_wait();
 

@@ -247,17 +247,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
-// Ask L2 to fetch the box of a 2-D tiled load at {x, y} ahead of the load
-// itself (no data reaches this CTA; completion is not tracked).  L2 is the
-// GPU's point of coherence, so a prefetch issued before griddepcontrol.wait
-// cannot make a later load see stale data: it only warms the cache.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tmap)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 // 2-D tiled store shared -> global (out-of-range rows/columns are clipped by TMA).
 __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
