@@ -316,7 +316,8 @@ class PeerBroadcast:
         slots = (ctypes.c_void_p * (W * self.SLOTS))(*[ptrs[r][k] for r in range(W) for k in range(self.SLOTS)])
         flagp = (ctypes.c_void_p * W)(*[ptrs[r][self.SLOTS] for r in range(W)])
         handle = ctypes.c_void_p()
-        rc = self._lib.b200_bcast_create(self.rank, W, self.nbytes, slots, flagp, ctypes.byref(handle))
+        with torch.cuda.device(self.device):  # its copy streams belong to this device
+            rc = self._lib.b200_bcast_create(self.rank, W, self.nbytes, slots, flagp, ctypes.byref(handle))
         if rc != _lib.B200_OK:
             raise _lib.B200GemmError(rc, "b200_bcast_create")
         self._h = handle

@@ -3,16 +3,20 @@
 // the exchange's slots inside the kernel (b200_gemm.cu).
 #pragma once
 
+#include <cuda_runtime.h>
+
 #include <cstddef>
 #include <cstdint>
 
 namespace b200 {
 constexpr int kBcastSlots = 2;
 constexpr int kBcastMaxWorld = 8;
-// Each piece moves in this many parts: part k of every piece leaves rank 0
-// before part k + 1 of any, and a receiving rank forwards a part as soon as
-// it has landed, so forwarding overlaps rank 0's sending.
-constexpr int kBcastParts = 4;
+// Each piece moves in this many parts, and a receiving rank forwards a part
+// as soon as it has landed, so forwarding overlaps rank 0's sending.
+#ifndef B200_BCAST_PARTS
+#define B200_BCAST_PARTS 2
+#endif
+constexpr int kBcastParts = B200_BCAST_PARTS;
 }  // namespace b200
 
 struct b200_bcast {
@@ -20,6 +24,12 @@ struct b200_bcast {
   size_t nbytes;
   char* slot[b200::kBcastMaxWorld][b200::kBcastSlots];  // every rank's slots as mapped in this process
   char* flags[b200::kBcastMaxWorld];                    // every rank's flag array as mapped in this process
+  // One copy stream per peer this rank writes to (copies to different peers
+  // run at the same time on different copy engines), and events to join them
+  // with the caller's stream.
+  cudaStream_t peer_stream[b200::kBcastMaxWorld];
+  cudaEvent_t start_ev;
+  cudaEvent_t done_ev[b200::kBcastMaxWorld];
 };
 
 namespace b200 {

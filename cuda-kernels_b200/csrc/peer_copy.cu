@@ -92,9 +92,10 @@ extern "C" B200_API int b200_wait_u32(const void* flag, uint32_t value, void* st
 // that slot has landed (value step + 1); done[rank] — that rank has finished
 // reading its slot of a step (value step + 1).  Pieces: the buffer is cut
 // into world - 1 pieces (b200_bcast_piece), each moved in kBcastParts parts;
-// rank 0 sends piece q-1 to rank q, part by part across all pieces, and rank
-// q forwards each part to every other receiving rank as soon as it has
-// landed, so every byte leaves rank 0 once and forwarding overlaps sending.  Before writing into a peer's slot for step s, a writer waits
+// rank 0 sends piece q-1 to rank q, and rank q forwards each part to every
+// other receiving rank as soon as it has landed, so every byte leaves rank 0
+// once and forwarding overlaps sending.  Copies to different peers go on
+// different streams (different copy engines), so they run at the same time.  Before writing into a peer's slot for step s, a writer waits
 // until that peer is done with step s - kSlots, which used the same slot.
 // ---------------------------------------------------------------------------
 namespace {
@@ -151,11 +152,29 @@ extern "C" B200_API int b200_bcast_create(int rank, int world, size_t nbytes, vo
       return B200_ERR_INVALID_ARG;
     }
   }
+  bool ok = cudaEventCreateWithFlags(&b->start_ev, cudaEventDisableTiming) == cudaSuccess;
+  for (int r = 0; ok && r < world; ++r) {
+    ok = cudaStreamCreateWithFlags(&b->peer_stream[r], cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreateWithFlags(&b->done_ev[r], cudaEventDisableTiming) == cudaSuccess;
+  }
+  if (!ok) {
+    cudaGetLastError();
+    b200_bcast_destroy(b);
+    return B200_ERR_CUDA;
+  }
   *out = b;
   return B200_OK;
 }
 
-extern "C" B200_API void b200_bcast_destroy(b200_bcast* b) { delete b; }
+extern "C" B200_API void b200_bcast_destroy(b200_bcast* b) {
+  if (b == nullptr) return;
+  for (int r = 0; r < b->world; ++r) {
+    if (b->peer_stream[r] != nullptr) cudaStreamDestroy(b->peer_stream[r]);
+    if (b->done_ev[r] != nullptr) cudaEventDestroy(b->done_ev[r]);
+  }
+  if (b->start_ev != nullptr) cudaEventDestroy(b->start_ev);
+  delete b;
+}
 
 extern "C" B200_API int b200_bcast_issue(b200_bcast* b, int64_t step, const void* src, void* stream) {
   if (b == nullptr) return B200_ERR_INVALID_ARG;
@@ -172,38 +191,55 @@ extern "C" B200_API int b200_bcast_issue_range(b200_bcast* b, int64_t step, cons
   const bool reuse = step >= kBcastSlots;  // the slot held step - kSlots: wait until its reader is done
   const uint32_t v_prev = (uint32_t)(step - kBcastSlots + 1);
   int rc;
+  // Every destination gets its own copy stream, started after the work
+  // already on `stream` (rank 0's source is ready) and joined back into it.
+  if (cudaEventRecord(b->start_ev, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return B200_ERR_CUDA;
+  auto fork = [&](int dst) -> void* {
+    return cudaStreamWaitEvent(b->peer_stream[dst], b->start_ev, 0) == cudaSuccess ? (void*)b->peer_stream[dst]
+                                                                                    : nullptr;
+  };
+  auto join = [&](int dst) -> int {
+    if (cudaEventRecord(b->done_ev[dst], b->peer_stream[dst]) != cudaSuccess ||
+        cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), b->done_ev[dst], 0) != cudaSuccess)
+      return B200_ERR_CUDA;
+    return B200_OK;
+  };
   if (b->rank == 0) {
     if (src == nullptr) return B200_ERR_INVALID_ARG;
-    // part k of every piece, then part k + 1: every receiver can start
-    // forwarding after the first round
-    for (int k = 0; k < kBcastParts; ++k) {
-      for (int q = 1; q < b->world; ++q) {
-        size_t off, len, poff, plen;
-        if ((rc = b200_bcast_piece(b->world, length, q - 1, &off, &len)) != B200_OK) return rc;
+    for (int q = 1; q < b->world; ++q) {
+      void* ps = fork(q);
+      if (ps == nullptr) return B200_ERR_CUDA;
+      size_t off, len;
+      if ((rc = b200_bcast_piece(b->world, length, q - 1, &off, &len)) != B200_OK) return rc;
+      if (reuse && (rc = b200_wait_u32(done_flag(b, 0, q), v_prev, ps)) != B200_OK) return rc;
+      for (int k = 0; k < kBcastParts; ++k) {
+        size_t poff, plen;
         piece_part(offset + off, len, k, &poff, &plen);
-        if (k == 0 && reuse && (rc = b200_wait_u32(done_flag(b, 0, q), v_prev, stream)) != B200_OK) return rc;
-        if ((rc = b200_copy_async(b->slot[q][slot] + poff, static_cast<const char*>(src) + poff, plen, stream)) !=
-            B200_OK)
+        if ((rc = b200_copy_async(b->slot[q][slot] + poff, static_cast<const char*>(src) + poff, plen, ps)) != B200_OK)
           return rc;
-        if ((rc = b200_signal_u32(ready_flag(b, q, slot, 0, k), v, stream)) != B200_OK) return rc;
+        if ((rc = b200_signal_u32(ready_flag(b, q, slot, 0, k), v, ps)) != B200_OK) return rc;
       }
+      if ((rc = join(q)) != B200_OK) return rc;
     }
     return B200_OK;
   }
   size_t off, len;
   if ((rc = b200_bcast_piece(b->world, length, b->rank - 1, &off, &len)) != B200_OK) return rc;
-  for (int k = 0; k < kBcastParts; ++k) {
-    size_t poff, plen;
-    piece_part(offset + off, len, k, &poff, &plen);
-    // part k of my piece has landed: pass it on
-    if ((rc = b200_wait_u32(ready_flag(b, b->rank, slot, 0, k), v, stream)) != B200_OK) return rc;
-    for (int r = 1; r < b->world; ++r) {
-      if (r == b->rank) continue;
-      if (k == 0 && reuse && (rc = b200_wait_u32(done_flag(b, b->rank, r), v_prev, stream)) != B200_OK) return rc;
-      if ((rc = b200_copy_async(b->slot[r][slot] + poff, b->slot[b->rank][slot] + poff, plen, stream)) != B200_OK)
+  for (int r = 1; r < b->world; ++r) {
+    if (r == b->rank) continue;
+    void* ps = fork(r);
+    if (ps == nullptr) return B200_ERR_CUDA;
+    if (reuse && (rc = b200_wait_u32(done_flag(b, b->rank, r), v_prev, ps)) != B200_OK) return rc;
+    for (int k = 0; k < kBcastParts; ++k) {
+      size_t poff, plen;
+      piece_part(offset + off, len, k, &poff, &plen);
+      // part k of my piece has landed: pass it on
+      if ((rc = b200_wait_u32(ready_flag(b, b->rank, slot, 0, k), v, ps)) != B200_OK) return rc;
+      if ((rc = b200_copy_async(b->slot[r][slot] + poff, b->slot[b->rank][slot] + poff, plen, ps)) != B200_OK)
         return rc;
-      if ((rc = b200_signal_u32(ready_flag(b, r, slot, b->rank, k), v, stream)) != B200_OK) return rc;
+      if ((rc = b200_signal_u32(ready_flag(b, r, slot, b->rank, k), v, ps)) != B200_OK) return rc;
     }
+    if ((rc = join(r)) != B200_OK) return rc;
   }
   return B200_OK;
 }
