@@ -64,7 +64,17 @@ static_assert(128 * kAttnRegsOther + kAttnQTiles * 128 * kAttnRegsSoftmax <= kAt
 // Every kAttnPolyEvery-th pair of exponentials on the FMA pipe (0: none).
 // Measured on B200: every 4th pair cost 2 %, every 2nd 7 % (the softmax is
 // bound by latency and issue, not by the MUFU rate), so it is off.
-constexpr int kAttnPolyEvery = 0;
+#ifndef B200_ATTN_POLY_EVERY
+#define B200_ATTN_POLY_EVERY 0
+#endif
+constexpr int kAttnPolyEvery = B200_ATTN_POLY_EVERY;
+// Exponential phases of the two softmax warpgroups in turn (tile 0 step j,
+// tile 1 step j, tile 0 step j+1, ...), each with the SM's MUFU to itself,
+// instead of both at once at half rate.
+#ifndef B200_ATTN_PINGPONG
+#define B200_ATTN_PINGPONG 0
+#endif
+constexpr bool kAttnPingPong = B200_ATTN_PINGPONG != 0;
 constexpr float kAttnRescaleLog2 = 8.0f;  // lazy rescale threshold (P stays <= 2^8)
 
 struct AttnParams {
@@ -87,8 +97,8 @@ struct AttnSmemPlan {
   static constexpr int kOffK = kOffQ + kAttnQTiles * kTileBytes;
   static constexpr int kOffV = kOffK + kAttnStages * kTileBytes;
   static constexpr int kOffBar = kOffV + kAttnStages * kTileBytes;
-  // q_full[Q], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[Q], p_full[Q][2], o_full[Q], drain
-  static constexpr int kNumBars = 5 * kAttnQTiles + 4 * kAttnStages + 1;
+  // q_full[Q], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[Q], p_full[Q][2], o_full[Q], drain, ex_done[Q]
+  static constexpr int kNumBars = 6 * kAttnQTiles + 4 * kAttnStages + 1;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAbort = kOffTmemHolder + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -197,6 +207,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto p_full = [&](int i, int h) { return bar0 + 8u * (2 * kAttnQTiles + 4 * kAttnStages + 2 * i + h); };
   auto o_full = [&](int i) { return bar0 + 8u * (4 * kAttnQTiles + 4 * kAttnStages + i); };
   const uint32_t drain = bar0 + 8u * (5 * kAttnQTiles + 4 * kAttnStages);  // every MMA issued has completed
+  // Softmax warpgroup i has finished the exponentials of a key tile.
+  auto ex_done = [&](int i) { return bar0 + 8u * (5 * kAttnQTiles + 4 * kAttnStages + 1 + i); };
   volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
 
@@ -234,6 +246,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(p_full(i, 0), 4);
       mbar_init(p_full(i, 1), 4);
       mbar_init(o_full(i), 1);
+      mbar_init(ex_done(i), 4);
     }
     for (int s = 0; s < kAttnStages; ++s) {
       mbar_init(k_full(s), 1);
@@ -490,6 +503,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l *= factor;
         m = m_new;
       }
+      if (kAttnPingPong && n_q == 2) {
+        // Wait for the phase before this one in the order above: tile 1's
+        // step j - 1 (for tile 0), tile 0's step j (for tile 1), when the
+        // other tile has that step.  The other tile is never more than one
+        // phase of its barrier ahead, so the parity wait cannot alias.
+        const int prev = tile == 0 ? j - 1 : j;
+        const int n_other = tile == 0 ? n1 : n0;
+        if (prev >= 0 && prev < n_other) {
+          const bool turn = mbar_wait(ex_done(tile ^ 1), (uint32_t)prev & 1u, p.timeout_ns, abort_flag);
+          if (!__all_sync(0xffffffffu, turn)) {
+            ok = false;
+            break;
+          }
+        }
+      }
       // P row -> TMEM over the first 64 columns of S (two bf16 per column),
       // in two halves of 64 keys, each published as soon as it is stored.
 #pragma unroll
@@ -503,6 +531,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(tile, h));
       }
+      if (kAttnPingPong && lane == 0) mbar_arrive(ex_done(tile));
     }
     if (!ok) {
       if (lane == 0) attn_raise(p, abort_flag, kDevTimeoutEpilogue);
