@@ -51,7 +51,17 @@ constexpr int kAttnD = 128;      // head dimension
 constexpr int kAttnBQ = 128;     // query rows per tile (UMMA M, TMEM lanes)
 constexpr int kAttnBKV = 128;    // keys per tile
 constexpr int kAttnQTiles = 2;   // query tiles per CTA, one softmax warpgroup each
-constexpr int kAttnStages = 2;   // K and V ring depth
+#ifndef B200_ATTN_K_STAGES
+#define B200_ATTN_K_STAGES 2
+#endif
+#ifndef B200_ATTN_V_STAGES
+#define B200_ATTN_V_STAGES 2
+#endif
+// K and V ring depths.  A third stage of either (the shared memory has room
+// for one) measured the same on B200, with or without the softmax: the
+// loads are not what the tensor pipe waits for.
+constexpr int kAttnKStages = B200_ATTN_K_STAGES;
+constexpr int kAttnVStages = B200_ATTN_V_STAGES;
 constexpr int kAttnThreads = 128 * (kAttnQTiles + 1);
 constexpr int kAttnProducerWarp = 4 * kAttnQTiles;
 constexpr int kAttnMmaWarp = kAttnProducerWarp + 1;
@@ -63,18 +73,15 @@ static_assert(128 * kAttnRegsOther + kAttnQTiles * 128 * kAttnRegsSoftmax <= kAt
               "register reallocation exceeds the launch pool");
 // Every kAttnPolyEvery-th pair of exponentials on the FMA pipe (0: none).
 // Measured on B200: every 4th pair cost 2 %, every 2nd 7 % (the softmax is
-// bound by latency and issue, not by the MUFU rate), so it is off.
+// bound by latency and issue, not by the MUFU rate), so it is off.  Neither
+// did taking turns help (the two softmax warpgroups' exponential phases one
+// after the other through an mbarrier, each with the MUFU to itself: 2-5 %
+// slower), nor splitting each row over two warpgroups of 64 keys each (their
+// maxima exchanged through shared memory: 7 % slower).
 #ifndef B200_ATTN_POLY_EVERY
 #define B200_ATTN_POLY_EVERY 0
 #endif
 constexpr int kAttnPolyEvery = B200_ATTN_POLY_EVERY;
-// Exponential phases of the two softmax warpgroups in turn (tile 0 step j,
-// tile 1 step j, tile 0 step j+1, ...), each with the SM's MUFU to itself,
-// instead of both at once at half rate.
-#ifndef B200_ATTN_PINGPONG
-#define B200_ATTN_PINGPONG 0
-#endif
-constexpr bool kAttnPingPong = B200_ATTN_PINGPONG != 0;
 constexpr float kAttnRescaleLog2 = 8.0f;  // lazy rescale threshold (P stays <= 2^8)
 
 struct AttnParams {
@@ -95,10 +102,11 @@ struct AttnSmemPlan {
   static constexpr int kTileBytes = 128 * 128 * 2;  // any 128 x 128 bf16 tile: 32 KiB
   static constexpr int kOffQ = 0;                   // kAttnQTiles tiles; O staging at the end
   static constexpr int kOffK = kOffQ + kAttnQTiles * kTileBytes;
-  static constexpr int kOffV = kOffK + kAttnStages * kTileBytes;
-  static constexpr int kOffBar = kOffV + kAttnStages * kTileBytes;
-  // q_full[Q], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[Q], p_full[Q][2], o_full[Q], drain, ex_done[Q]
-  static constexpr int kNumBars = 6 * kAttnQTiles + 4 * kAttnStages + 1;
+  static constexpr int kOffV = kOffK + kAttnKStages * kTileBytes;
+  static constexpr int kOffBar = kOffV + kAttnVStages * kTileBytes;
+  // q_full[Q], k_full[KS], k_empty[KS], v_full[VS], v_empty[VS], s_full[Q], p_full[Q][2], o_full[Q], drain
+  static constexpr int kRingBars = kAttnQTiles + 2 * kAttnKStages + 2 * kAttnVStages;
+  static constexpr int kNumBars = kRingBars + 4 * kAttnQTiles + 1;
   static constexpr int kOffTmemHolder = kOffBar + kNumBars * 8;
   static constexpr int kOffAbort = kOffTmemHolder + 4;
   static constexpr int kBytes = kOffAbort + 4;
@@ -199,16 +207,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t bar0 = base + Plan::kOffBar;
   auto q_full = [&](int i) { return bar0 + 8u * i; };
   auto k_full = [&](int s) { return bar0 + 8u * (kAttnQTiles + s); };
-  auto k_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + kAttnStages + s); };
-  auto v_full = [&](int s) { return bar0 + 8u * (kAttnQTiles + 2 * kAttnStages + s); };
-  auto v_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + 3 * kAttnStages + s); };
-  auto s_full = [&](int i) { return bar0 + 8u * (kAttnQTiles + 4 * kAttnStages + i); };
+  auto k_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + kAttnKStages + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (kAttnQTiles + 2 * kAttnKStages + s); };
+  auto v_empty = [&](int s) { return bar0 + 8u * (kAttnQTiles + 2 * kAttnKStages + kAttnVStages + s); };
+  auto s_full = [&](int i) { return bar0 + 8u * (Plan::kRingBars + i); };
   // P of tile i, keys 64 h .. 64 h + 63, in TMEM.
-  auto p_full = [&](int i, int h) { return bar0 + 8u * (2 * kAttnQTiles + 4 * kAttnStages + 2 * i + h); };
-  auto o_full = [&](int i) { return bar0 + 8u * (4 * kAttnQTiles + 4 * kAttnStages + i); };
-  const uint32_t drain = bar0 + 8u * (5 * kAttnQTiles + 4 * kAttnStages);  // every MMA issued has completed
-  // Softmax warpgroup i has finished the exponentials of a key tile.
-  auto ex_done = [&](int i) { return bar0 + 8u * (5 * kAttnQTiles + 4 * kAttnStages + 1 + i); };
+  auto p_full = [&](int i, int h) { return bar0 + 8u * (Plan::kRingBars + kAttnQTiles + 2 * i + h); };
+  auto o_full = [&](int i) { return bar0 + 8u * (Plan::kRingBars + 3 * kAttnQTiles + i); };
+  const uint32_t drain = bar0 + 8u * (Plan::kRingBars + 4 * kAttnQTiles);  // every MMA issued has completed
+  // Ring slot and phase parity of key tile j.
+  auto k_slot = [](int j) { return j % kAttnKStages; };
+  auto k_par = [](int j) { return (uint32_t)(j / kAttnKStages) & 1u; };
+  auto v_slot = [](int j) { return j % kAttnVStages; };
+  auto v_par = [](int j) { return (uint32_t)(j / kAttnVStages) & 1u; };
   volatile uint32_t* tmem_holder = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffTmemHolder);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(base_ptr + Plan::kOffAbort);
 
@@ -246,11 +257,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(p_full(i, 0), 4);
       mbar_init(p_full(i, 1), 4);
       mbar_init(o_full(i), 1);
-      mbar_init(ex_done(i), 4);
     }
-    for (int s = 0; s < kAttnStages; ++s) {
+    for (int s = 0; s < kAttnKStages; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
+    }
+    for (int s = 0; s < kAttnVStages; ++s) {
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
@@ -290,27 +302,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         bool ok = true;
         int k_issued = 0, v_issued = 0;
         for (int j = 0; j < n_max && ok; ++j) {
-          const int s = j & 1;
-          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-          if (!mbar_wait(k_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
+          const int sk = k_slot(j), sv = v_slot(j);
+          if (!mbar_wait(k_empty(sk), k_par(j) ^ 1u, p.timeout_ns, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(k_full(s), Plan::kTileBytes);
+          mbar_arrive_expect_tx(k_full(sk), Plan::kTileBytes);
           for (int h = 0; h < 2; ++h) {
-            tma_load_3d(sK + s * Plan::kTileBytes + h * 16384, &tmK, k_full(s), kv_col0 + 64 * h, j * kAttnBKV, bat,
-                        pol_keep);
+            tma_load_3d(sK + sk * Plan::kTileBytes + h * 16384, &tmK, k_full(sk), kv_col0 + 64 * h, j * kAttnBKV,
+                        bat, pol_keep);
           }
           ++k_issued;
-          if (!mbar_wait(v_empty(s), ph ^ 1u, p.timeout_ns, abort_flag)) {
+          if (!mbar_wait(v_empty(sv), v_par(j) ^ 1u, p.timeout_ns, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(v_full(s), Plan::kTileBytes);
+          mbar_arrive_expect_tx(v_full(sv), Plan::kTileBytes);
           // V tile as two 64-key halves, each two 64-column atoms of [64 keys][64 d].
           for (int hk = 0; hk < 2; ++hk) {
             for (int h = 0; h < 2; ++h) {
-              tma_load_3d(sV + s * Plan::kTileBytes + hk * 16384 + h * 8192, &tmV, v_full(s), kv_col0 + 64 * h,
+              tma_load_3d(sV + sv * Plan::kTileBytes + hk * 16384 + h * 8192, &tmV, v_full(sv), kv_col0 + 64 * h,
                           j * kAttnBKV + 64 * hk, bat, pol_keep);
             }
           }
@@ -320,11 +331,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // Let the copies in flight land before the CTA can leave.
         bool drained = true;
         for (int i = 0; drained && i < n_q; ++i) drained = mbar_wait(q_full(i), 0u, p.timeout_ns, nullptr);
-        for (int j = k_issued - 1; drained && j >= 0 && j >= k_issued - kAttnStages; --j) {
-          drained = mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
+        for (int j = k_issued - 1; drained && j >= 0 && j >= k_issued - kAttnKStages; --j) {
+          drained = mbar_wait(k_full(k_slot(j)), k_par(j), p.timeout_ns, nullptr);
         }
-        for (int j = v_issued - 1; drained && j >= 0 && j >= v_issued - kAttnStages; --j) {
-          drained = mbar_wait(v_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, nullptr);
+        for (int j = v_issued - 1; drained && j >= 0 && j >= v_issued - kAttnVStages; --j) {
+          drained = mbar_wait(v_full(v_slot(j)), v_par(j), p.timeout_ns, nullptr);
         }
         if (!drained) attn_raise(p, abort_flag, kDevTimeoutDrain);
       }
@@ -346,7 +357,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         };
         auto issue_s = [&](int i, int j) {
           const uint32_t qa = sQ + (uint32_t)(i * Plan::kTileBytes);
-          const uint32_t kt = sK + (uint32_t)((j & 1) * Plan::kTileBytes);
+          const uint32_t kt = sK + (uint32_t)(k_slot(j) * Plan::kTileBytes);
 #pragma unroll
           for (int k = 0; k < kAttnD / kUmmaK; ++k) {
             umma_bf16(tmem_base + (uint32_t)(i * 128), kmajor(qa, k), kmajor(kt, k), idesc_s, k > 0 ? 1u : 0u);
@@ -354,14 +365,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         };
         // Keys 64 h .. 64 h + 63 of P V (K slices 4 h .. 4 h + 3).
         auto issue_pv = [&](int i, int j, int h) {
-          const uint32_t vt = sV + (uint32_t)((j & 1) * Plan::kTileBytes);
+          const uint32_t vt = sV + (uint32_t)(v_slot(j) * Plan::kTileBytes);
 #pragma unroll
           for (int k = 4 * h; k < 4 * h + 4; ++k) {
             umma_bf16_ts(tmem_base + 256u + (uint32_t)(i * 128), tmem_base + (uint32_t)(i * 128 + k * 8),
                          vdesc(vt, k), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
           }
         };
-        auto wait_k = [&](int j) { return mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag); };
+        auto wait_k = [&](int j) { return mbar_wait(k_full(k_slot(j)), k_par(j), p.timeout_ns, abort_flag); };
         bool ok = true;
         for (int i = 0; ok && i < n_q; ++i) ok = mbar_wait(q_full(i), 0u, p.timeout_ns, abort_flag);
         if (ok && n_max > 0) {
@@ -377,8 +388,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const int n_tiles[2] = {n0, n1};
         for (int j = 0; j < n_max && ok; ++j) {
-          const int s = j & 1;
-          if (!mbar_wait(v_full(s), (uint32_t)(j >> 1) & 1u, p.timeout_ns, abort_flag)) {
+          if (!mbar_wait(v_full(v_slot(j)), v_par(j), p.timeout_ns, abort_flag)) {
             ok = false;
             break;
           }
@@ -400,7 +410,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
             tc_fence_after();
             issue_pv(i, j, 1);
-            if (i == kAttnQTiles - 1 || j >= n_tiles[kAttnQTiles - 1]) umma_commit(v_empty(s));  // last user of V_j
+            if (i == kAttnQTiles - 1 || j >= n_tiles[kAttnQTiles - 1]) umma_commit(v_empty(v_slot(j)));  // last user of V_j
             if (j + 1 < n_tiles[i]) {
               if (!k_ready) {
                 if (!wait_k(j + 1)) {
@@ -416,7 +426,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               umma_commit(o_full(i));
             }
           }
-          if (ok && j + 1 < n_max) umma_commit(k_empty((j + 1) & 1));
+          if (ok && j + 1 < n_max) umma_commit(k_empty(k_slot(j + 1)));
         }
         if (!ok) attn_raise(p, abort_flag, kDevTimeoutMma);
         umma_commit(drain);
@@ -503,21 +513,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l *= factor;
         m = m_new;
       }
-      if (kAttnPingPong && n_q == 2) {
-        // Wait for the phase before this one in the order above: tile 1's
-        // step j - 1 (for tile 0), tile 0's step j (for tile 1), when the
-        // other tile has that step.  The other tile is never more than one
-        // phase of its barrier ahead, so the parity wait cannot alias.
-        const int prev = tile == 0 ? j - 1 : j;
-        const int n_other = tile == 0 ? n1 : n0;
-        if (prev >= 0 && prev < n_other) {
-          const bool turn = mbar_wait(ex_done(tile ^ 1), (uint32_t)prev & 1u, p.timeout_ns, abort_flag);
-          if (!__all_sync(0xffffffffu, turn)) {
-            ok = false;
-            break;
-          }
-        }
-      }
       // P row -> TMEM over the first 64 columns of S (two bf16 per column),
       // in two halves of 64 keys, each published as soon as it is stored.
 #pragma unroll
@@ -531,7 +526,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(tile, h));
       }
-      if (kAttnPingPong && lane == 0) mbar_arrive(ex_done(tile));
     }
     if (!ok) {
       if (lane == 0) attn_raise(p, abort_flag, kDevTimeoutEpilogue);
