@@ -34,6 +34,10 @@ B200_KERNEL_SINGLE = 1
 B200_KERNEL_PAIR = 2
 B200_KERNEL_SKINNY = 3
 
+B200_ATTN_KERNEL_AUTO = 0
+B200_ATTN_KERNEL_SINGLE = 1
+B200_ATTN_KERNEL_PAIR = 2
+
 class Epilogue(ctypes.Structure):
     """struct b200_epilogue (include/b200_gemm.h)."""
     _fields_ = [("alpha", ctypes.c_float), ("beta", ctypes.c_float), ("c_in", ctypes.c_void_p),
@@ -98,6 +102,7 @@ _SIGNATURES = {
     "b200_gemm_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "b200_gemm_set_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "b200_gemm_set_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "b200_flash_attn_set_kernel": (ctypes.c_int, [ctypes.c_int]),
     "b200_gemm_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "b200_gemm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "b200_gemm_version": (ctypes.c_char_p, []),

@@ -268,3 +268,17 @@ def set_kernel(which: str) -> None:
     if rc != _lib.B200_OK:
         raise B200GemmError(rc)
 
+
+_ATTN_KERNELS = {"auto": _lib.B200_ATTN_KERNEL_AUTO, "single": _lib.B200_ATTN_KERNEL_SINGLE,
+                 "pair": _lib.B200_ATTN_KERNEL_PAIR}
+
+
+def flash_attn_set_kernel(which: str) -> None:
+    """Force the attention kernel for later flash_attn calls ("auto", "single": one CTA per two query
+    tiles, "pair": a CTA pair per four); for tests and tuning, every choice computes the same result."""
+    if which not in _ATTN_KERNELS:
+        raise ValueError(f"attention kernel must be one of {sorted(_ATTN_KERNELS)}")
+    rc = _lib.load().b200_flash_attn_set_kernel(_ATTN_KERNELS[which])
+    if rc != _lib.B200_OK:
+        raise B200GemmError(rc)
+

@@ -24,6 +24,7 @@
 #include "gemm_sm100_skinny.cuh"
 #include "split_f32.cuh"
 #include "attn_sm100.cuh"
+#include "attn_sm100_pair.cuh"
 #include "peer_bcast.h"
 
 namespace {
@@ -72,6 +73,7 @@ constexpr int kMaxClusterSplits = 8;  // portable cluster size limit
 // Kernel selection override (b200_gemm_set_kernel): process-wide.
 enum ForceKernel { kForceAuto = 0, kForceSingle = 1, kForcePair = 2, kForceSkinny = 3 };
 std::atomic<int> g_force_kernel{kForceAuto};
+std::atomic<int> g_attn_kernel{B200_ATTN_KERNEL_AUTO};
 
 struct DeviceState {
   std::once_flag once;
@@ -85,6 +87,7 @@ struct DeviceState {
   // shares add up to exactly the pool of a launch at kAttnRegsLaunch
   // registers per thread, so it only runs when the binary has that count.
   bool attn_regs_ok = false;
+  bool attn_pair_regs_ok = false;  // the same for the CTA-pair attention kernel
   // Same for the eight-epilogue-warp wide pair kernel (kWide8Regs*); when the
   // binary has another count, the four-warp wide kernel is used instead.
   bool wide8_regs_ok = false;
@@ -214,6 +217,14 @@ int init_device(int dev, DeviceState& st) {
     cudaFuncAttributes fa{};
     if (cudaFuncGetAttributes(&fa, b200::flash_attn_fwd_kernel) != cudaSuccess) return B200_ERR_CUDA;
     st.attn_regs_ok = fa.numRegs == (int)b200::kAttnRegsLaunch;
+  }
+  if (cudaFuncSetAttribute(b200::flash_attn_fwd_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           b200::AttnPairSmemPlan::kAllocBytes) != cudaSuccess)
+    return B200_ERR_CUDA;
+  {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, b200::flash_attn_fwd_pair_kernel) != cudaSuccess) return B200_ERR_CUDA;
+    st.attn_pair_regs_ok = fa.numRegs == (int)b200::kAttnRegsLaunch;
   }
   {
     st.wide8_regs_ok = true;
@@ -957,9 +968,16 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   if (!st->attn_regs_ok) return B200_ERR_CUDA;  // built with another register count: never launch it
   const uint64_t cols = (uint64_t)(heads * head_dim);
   const uint64_t kv_cols = (uint64_t)(kv_heads * head_dim);
+  // The CTA-pair kernel (each SM reading half of every K and V tile) only
+  // when asked for: on B200 it measured slower than the one-CTA kernel at
+  // every size (attn_sm100_pair.cuh).
+  const bool pair = g_attn_kernel.load(std::memory_order_relaxed) == B200_ATTN_KERNEL_PAIR;
+  if (pair && !st->attn_pair_regs_ok) return B200_ERR_CUDA;  // built with another register count
+  if (pair && 2 * heads * batch > 0x7fffffffLL) return B200_ERR_TOO_LARGE;
   CUtensorMap tmQ, tmK, tmV, tmO;
   if ((rc = encode_3d(&tmQ, Q, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 128, true)) != B200_OK ||
-      (rc = encode_3d(&tmK, K, kv_cols, (uint64_t)seq_len, (uint64_t)batch, kv_cols, 64, 128, true)) != B200_OK ||
+      (rc = encode_3d(&tmK, K, kv_cols, (uint64_t)seq_len, (uint64_t)batch, kv_cols, 64, pair ? 64 : 128, true)) !=
+          B200_OK ||
       (rc = encode_3d(&tmV, V, kv_cols, (uint64_t)seq_len, (uint64_t)batch, kv_cols, 64, 64, true)) != B200_OK ||
       (rc = encode_3d(&tmO, O, cols, (uint64_t)seq_len, (uint64_t)batch, cols, 64, 32, false)) != B200_OK)
     return rc;
@@ -981,9 +999,25 @@ extern "C" B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const
   p.timeout_ns = st->timeout_ns;
   p.status = st->status_ptr;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (pair) {
+    p.balanced = 0u;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(2 * heads * batch), (unsigned)((p.num_q_tiles + 3) / 4), 1);
+    cfg.blockDim = dim3(b200::kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = b200::AttnPairSmemPlan::kAllocBytes;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream_);
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, b200::flash_attn_fwd_pair_kernel, tmQ, tmK, tmV, tmO, p) == cudaSuccess
+               ? B200_OK
+               : B200_ERR_CUDA;
+  }
   cfg.gridDim = dim3((unsigned)(heads * batch), (unsigned)((p.num_q_tiles + b200::kAttnQTiles - 1) / b200::kAttnQTiles),
                      1);
   cfg.blockDim = dim3(b200::kAttnThreads, 1, 1);
@@ -1079,6 +1113,12 @@ extern "C" B200_API int b200_gemm_selftest_wait_timeout(uint64_t timeout_ns, voi
   if (timeout_ns == 0 || timeout_ns > 10000000000ull) return B200_ERR_INVALID_ARG;
   selftest_wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(timeout_ns, st->status_ptr);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+extern "C" B200_API int b200_flash_attn_set_kernel(int which) {
+  if (which < B200_ATTN_KERNEL_AUTO || which > B200_ATTN_KERNEL_PAIR) return B200_ERR_INVALID_ARG;
+  g_attn_kernel.store(which, std::memory_order_relaxed);
+  return B200_OK;
 }
 
 extern "C" B200_API int b200_gemm_set_kernel(int which) {

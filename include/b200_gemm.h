@@ -237,6 +237,22 @@ B200_API int b200_flash_attn_bf16(const void* Q, const void* K, const void* V, v
                                   int64_t seq_len, int64_t heads, int64_t kv_heads, int64_t head_dim, int causal,
                                   void* stream);
 
+/*
+ * Attention kernel selection for later b200_flash_attn_bf16 calls in this
+ * process (all devices):
+ *   B200_ATTN_KERNEL_AUTO   (0) default: the faster kernel, on B200 SINGLE
+ *   B200_ATTN_KERNEL_SINGLE (1) one CTA per two 128-row query tiles
+ *   B200_ATTN_KERNEL_PAIR   (2) a CTA pair per four query tiles (cta_group::2
+ *                               products, each SM holding half of every K and
+ *                               V tile; slower on B200)
+ * For testing and tuning; every choice computes the same attention.  No
+ * reference counterpart (the reference has one attention kernel).
+ */
+#define B200_ATTN_KERNEL_AUTO 0
+#define B200_ATTN_KERNEL_SINGLE 1
+#define B200_ATTN_KERNEL_PAIR 2
+B200_API int b200_flash_attn_set_kernel(int which);
+
 /* Element type of D for b200_gemm_bf16_ex. */
 #define B200_DTYPE_BF16 0
 #define B200_DTYPE_F32 1

@@ -118,6 +118,9 @@ def test_attention_argument_errors_without_gpu():
     assert f(fake, None, fake, fake, 1, 128, 2, 2, 128, 1, None) == _lib.B200_ERR_INVALID_ARG
     assert f(fake, fake, P(0x10008), fake, 1, 128, 2, 2, 128, 1, None) == _lib.B200_ERR_ALIGNMENT
     assert f(fake, fake, fake, fake, 0, 128, 2, 2, 128, 1, None) == _lib.B200_OK  # empty: nothing to do
+    assert lib.b200_flash_attn_set_kernel(3) == _lib.B200_ERR_INVALID_ARG
+    assert lib.b200_flash_attn_set_kernel(-1) == _lib.B200_ERR_INVALID_ARG
+    assert lib.b200_flash_attn_set_kernel(_lib.B200_ATTN_KERNEL_AUTO) == _lib.B200_OK
 
 
 def test_epilogue_argument_errors_without_gpu():

@@ -7,7 +7,9 @@ Covers causal and full masks, ragged sequence lengths (tiles of 128), several
 batches and heads, grouped-query attention (fewer key/value heads than query
 heads, as the reference's kernel allows), the reference-shaped torch binding
 (fa2_tma_lazy_rescale), and scores that grow along the keys so the lazy
-rescaling of the running max is exercised."""
+rescaling of the running max is exercised.  The exact-oracle cases run on
+both kernels (one CTA per two query tiles, and CTA pairs per four), forced
+through flash_attn_set_kernel; the automatic choice is covered by the rest."""
 import os
 
 import numpy as np
@@ -24,6 +26,13 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+@pytest.fixture(params=["single", "pair"])
+def attn_kernel(request):
+    b200_gemm.flash_attn_set_kernel(request.param)
+    yield request.param
+    b200_gemm.flash_attn_set_kernel("auto")
+
+
 def _inputs(B, S, H, seed, grow=False, Hkv=None):
     Hkv = H if Hkv is None else Hkv
     g = torch.Generator().manual_seed(seed)
@@ -37,10 +46,10 @@ def _inputs(B, S, H, seed, grow=False, Hkv=None):
 
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("shape", [(1, 128, 2), (2, 384, 3), (1, 200, 2), (1, 1024, 4), (1, 77, 1), (1, 1, 2),
-                                   (3, 130, 5)],
+                                   (3, 130, 5), (1, 640, 2), (1, 2178, 2)],
                          ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("grow", [False, True])
-def test_attention_vs_exact(shape, causal, grow):
+def test_attention_vs_exact(shape, causal, grow, attn_kernel):
     B, S, H = shape
     q, k, v = _inputs(B, S, H, seed=B * 1000 + S + H, grow=grow)
     out = b200_gemm.flash_attn(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
@@ -55,9 +64,9 @@ def test_attention_vs_exact(shape, causal, grow):
 
 
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("shape", [(1, 256, 4, 2), (2, 200, 6, 1), (1, 384, 8, 4)],
+@pytest.mark.parametrize("shape", [(1, 256, 4, 2), (2, 200, 6, 1), (1, 384, 8, 4), (1, 1100, 4, 2)],
                          ids=lambda s: "x".join(map(str, s)))
-def test_grouped_query_attention_vs_exact(shape, causal):
+def test_grouped_query_attention_vs_exact(shape, causal, attn_kernel):
     B, S, H, Hkv = shape
     q, k, v = _inputs(B, S, H, seed=17 * S + H + Hkv, Hkv=Hkv)
     out = b200_gemm.flash_attn(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
