@@ -9,10 +9,9 @@ Importing the package loads the compiled C-ABI library and fails if it is
 missing: there is no fallback path.
 """
 from ._lib import B200GemmError, exported_symbols, load as _load_lib
-from .ops import (check_status, flash_attn, flash_attn_set_kernel, gemm, gemm_f32, matmul, set_b_readonly, set_kernel,
-                  set_timeout_ns)
+from .ops import check_status, flash_attn, flash_attn_set_kernel, gemm, gemm_f32, matmul, set_kernel, set_timeout_ns
 
 _load_lib()
 
 __all__ = ["B200GemmError", "check_status", "exported_symbols", "flash_attn", "flash_attn_set_kernel", "gemm", "gemm_f32",
-           "matmul", "set_b_readonly", "set_kernel", "set_timeout_ns"]
+           "matmul", "set_kernel", "set_timeout_ns"]

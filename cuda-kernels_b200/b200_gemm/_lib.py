@@ -103,7 +103,6 @@ _SIGNATURES = {
     "b200_gemm_set_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "b200_gemm_set_kernel": (ctypes.c_int, [ctypes.c_int]),
     "b200_flash_attn_set_kernel": (ctypes.c_int, [ctypes.c_int]),
-    "b200_gemm_set_b_readonly": (ctypes.c_int, [ctypes.c_int]),
     "b200_gemm_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "b200_gemm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "b200_gemm_version": (ctypes.c_char_p, []),

@@ -269,15 +269,6 @@ def set_kernel(which: str) -> None:
         raise B200GemmError(rc)
 
 
-def set_b_readonly(on: bool) -> None:
-    """Promise (for later calls, default off) that no earlier kernel in a call's stream writes its B
-    (weights): the M <= 128 kernel then starts loading B before the previous kernel has finished.
-    Same results; breaking the promise can read stale B."""
-    rc = _lib.load().b200_gemm_set_b_readonly(1 if on else 0)
-    if rc != _lib.B200_OK:
-        raise B200GemmError(rc)
-
-
 _ATTN_KERNELS = {"auto": _lib.B200_ATTN_KERNEL_AUTO, "single": _lib.B200_ATTN_KERNEL_SINGLE,
                  "pair": _lib.B200_ATTN_KERNEL_PAIR}
 

@@ -74,7 +74,6 @@ constexpr int kMaxClusterSplits = 8;  // portable cluster size limit
 enum ForceKernel { kForceAuto = 0, kForceSingle = 1, kForcePair = 2, kForceSkinny = 3 };
 std::atomic<int> g_force_kernel{kForceAuto};
 std::atomic<int> g_attn_kernel{B200_ATTN_KERNEL_AUTO};
-std::atomic<int> g_b_readonly{0};  // b200_gemm_set_b_readonly
 
 struct DeviceState {
   std::once_flag once;
@@ -383,7 +382,6 @@ int launch_skinny(const DeviceState& st, const void* A, const void* B, void* C, 
   if ((rc = encode_2d(&tmC, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, box_n, MPAD, false, false,
                       epi.out_f32 != 0)) != B200_OK)
     return rc;
-  p.b_early = g_b_readonly.load(std::memory_order_relaxed) != 0 ? 1u : 0u;
   p.timeout_ns = st.timeout_ns;
   p.status = st.status_ptr;
   p.epi = epi;
@@ -1115,12 +1113,6 @@ extern "C" B200_API int b200_gemm_selftest_wait_timeout(uint64_t timeout_ns, voi
   if (timeout_ns == 0 || timeout_ns > 10000000000ull) return B200_ERR_INVALID_ARG;
   selftest_wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(timeout_ns, st->status_ptr);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
-}
-
-extern "C" B200_API int b200_gemm_set_b_readonly(int on) {
-  if (on != 0 && on != 1) return B200_ERR_INVALID_ARG;
-  g_b_readonly.store(on, std::memory_order_relaxed);
-  return B200_OK;
 }
 
 extern "C" B200_API int b200_flash_attn_set_kernel(int which) {

@@ -36,10 +36,6 @@ struct SkinnyParams {
   int32_t num_k_blk;     // total K-blocks of 64
   int32_t kb_per_split;  // K-blocks per CTA of a cluster
   int32_t splits;        // S = cluster size along x: 1, 2, 4 or 8
-  // The caller promises that no earlier kernel in the stream writes B (the
-  // weights): the first ring's worth of B tiles is loaded before the launch
-  // wait, while the previous kernel is still finishing.
-  uint32_t b_early;
   uint64_t timeout_ns;
   uint32_t* status;
   EpilogueParams epi;  // fused epilogue (element [m, n] of D; see gemm_sm100.cuh)
@@ -181,8 +177,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // it before touching global memory, and let the next kernel start its own
   // prologue as early as possible.
   pdl_launch_dependents();
-  // With b_early the producer thread waits later, after its first B loads.
-  if (!(p.b_early != 0u && warp == 0 && lane == 0)) pdl_wait();
+  pdl_wait();
 
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
@@ -191,7 +186,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // by the CTAs of every tile: keep it.
       const uint64_t pol_b = l2_policy_evict_first();
       const uint64_t pol_a = l2_policy_evict_last();
-      auto load_b = [&](int stage, int kb, uint32_t fb) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = full_bar(stage);
+        mbar_arrive_expect_tx(fb, Plan::kStageBytes);
         const uint32_t dBt = sBt + stage * Plan::kBtBytes;
         if constexpr (!B_MN) {
           tma_load_2d(dBt, &tmB, fb, kb * kBK, n0, pol_b);
@@ -199,38 +204,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           tma_load_2d(dBt, &tmB, fb, n0, kb * kBK, pol_b);
           tma_load_2d(dBt + 64 * kBK * 2, &tmB, fb, n0 + 64, kb * kBK, pol_b);
         }
-      };
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued = 0;
-      bool ok = true;
-      int kb = kb_begin;
-      if (p.b_early != 0u) {
-        // The ring starts empty: B of its first stages now, the activation
-        // tiles (which the previous kernel may still be writing) after the
-        // launch wait.
-        const int pre = min(STAGES, my_kb);
-        for (int s = 0; s < pre; ++s) {
-          mbar_arrive_expect_tx(full_bar(s), Plan::kStageBytes);
-          load_b(s, kb_begin + s, full_bar(s));
-        }
-        pdl_wait();
-        for (int s = 0; s < pre; ++s) {
-          tma_load_2d(sAt + s * Plan::kAtBytes, &tmA, full_bar(s), (kb_begin + s) * kBK, 0, pol_a);
-        }
-        issued = (uint32_t)pre;
-        kb = kb_begin + pre;
-        stage = pre % STAGES;
-        phase = pre == STAGES ? 1u : 0u;
-      }
-      for (; kb < kb_end; ++kb) {
-        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const uint32_t fb = full_bar(stage);
-        mbar_arrive_expect_tx(fb, Plan::kStageBytes);
-        load_b(stage, kb, fb);
         tma_load_2d(sAt + stage * Plan::kAtBytes, &tmA, fb, kb * kBK, 0, pol_a);
         ++issued;
         if (++stage == STAGES) {

@@ -350,17 +350,6 @@ B200_API int b200_gemm_set_timeout_ns(uint64_t timeout_ns);
 B200_API int b200_gemm_set_kernel(int which);
 
 /*
- * Promise for later calls in this process (all devices), default off (0):
- * with on = 1 the caller guarantees that no kernel issued earlier in a call's
- * stream writes that call's B (model weights, written once before use).  The
- * M <= 128 kernel then loads its first B tiles before the launch wait, while
- * the previous kernel in the stream is still finishing, and only the
- * activation tiles wait for it.  Results are bit for bit the same; breaking
- * the promise can read stale B.  No reference counterpart.
- */
-B200_API int b200_gemm_set_b_readonly(int on);
-
-/*
  * Failure-detection self-test: launches one CTA that waits, with the same
  * bounded wait every GEMM kernel uses, on an mbarrier that nothing arrives at
  * (timeout_ns in (0, 1e10]).  The wait gives up after timeout_ns; the next

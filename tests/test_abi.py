@@ -121,8 +121,6 @@ def test_attention_argument_errors_without_gpu():
     assert lib.b200_flash_attn_set_kernel(3) == _lib.B200_ERR_INVALID_ARG
     assert lib.b200_flash_attn_set_kernel(-1) == _lib.B200_ERR_INVALID_ARG
     assert lib.b200_flash_attn_set_kernel(_lib.B200_ATTN_KERNEL_AUTO) == _lib.B200_OK
-    assert lib.b200_gemm_set_b_readonly(2) == _lib.B200_ERR_INVALID_ARG
-    assert lib.b200_gemm_set_b_readonly(0) == _lib.B200_OK
 
 
 def test_epilogue_argument_errors_without_gpu():
