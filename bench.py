@@ -710,8 +710,9 @@ class _Steps:
     """The headline job's steps.  N=1: one GEMM per step.  N>1: step s
     multiplies this rank's A panel by rank 0's B of step s, delivered by
     PeerBroadcast (copy engines over NVLink): while the GEMM of step s runs,
-    the B of step s+1 is already moving.  Step numbers count up across warm-up
-    and timed steps (the exchange's flags compare them)."""
+    the B of steps s+1 and s+2 are already moving (three receive slots; at 8
+    GPUs one exchange takes longer than one GEMM).  Step numbers count up
+    across warm-up and timed steps (the exchange's flags compare them)."""
 
     def __init__(self, b200_gemm, A, B, C, layout, world, rank, stream):
         self.g, self.A, self.B, self.C, self.layout = b200_gemm, A, B, C, layout
@@ -722,13 +723,15 @@ class _Steps:
             from b200_gemm.dist import PeerBroadcast
             nbytes = B[0].numel() * B[0].element_size()
             self.pb = PeerBroadcast(nbytes)
-            self.slot_views = [None, None]
+            self.ahead = self.pb.SLOTS - 1  # steps issued ahead of the one being multiplied
+            self.slot_views = [None] * self.pb.SLOTS
             if rank != 0:
-                self.slot_views = [self.pb.data(k).view(torch_bf16()).view(B[0].shape) for k in range(2)]
-            self.pb.issue(0, B[0] if rank == 0 else None)
+                self.slot_views = [self.pb.data(k).view(torch_bf16()).view(B[0].shape) for k in range(self.pb.SLOTS)]
+            for k in range(self.ahead):
+                self.pb.issue(k, B[k % ROTATE] if rank == 0 else None)
 
     def b_of(self, s):
-        return self.B[s % ROTATE] if (self.world == 1 or self.rank == 0) else self.slot_views[s % 2]
+        return self.B[s % ROTATE] if (self.world == 1 or self.rank == 0) else self.slot_views[s % self.pb.SLOTS]
 
     def __call__(self):
         s = self.s
@@ -737,7 +740,8 @@ class _Steps:
         if self.pb is None:
             self.g.gemm(self.A[j], self.B[j], b_layout=self.layout, out=self.C[j])
             return
-        self.pb.issue(s + 1, self.B[(s + 1) % ROTATE] if self.rank == 0 else None)
+        t = s + self.ahead
+        self.pb.issue(t, self.B[t % ROTATE] if self.rank == 0 else None)
         # waits for this step's B and releases its slot inside the GEMM kernel
         self.pb.gemm(s, self.A[j], tuple(self.B[0].shape), out=self.C[j], b_layout=self.layout,
                      src=self.B[j] if self.rank == 0 else None, stream=self.stream)
@@ -746,7 +750,8 @@ class _Steps:
         """One step of the B exchange alone (no GEMM): its cost on its own."""
         s = self.s
         self.s += 1
-        self.pb.issue(s + 1, self.B[(s + 1) % ROTATE] if self.rank == 0 else None)
+        t = s + self.ahead
+        self.pb.issue(t, self.B[t % ROTATE] if self.rank == 0 else None)
         self.pb.wait(s, self.stream)
         self.pb.release(s, self.stream)
 

@@ -25,6 +25,7 @@ B200_B_NK = 0
 B200_B_KN = 1
 
 B200_IPC_HANDLE_BYTES = 64
+B200_BCAST_SLOTS = 3
 
 B200_DTYPE_BF16 = 0
 B200_DTYPE_F32 = 1

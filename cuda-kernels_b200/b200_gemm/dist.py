@@ -34,6 +34,8 @@ from typing import Callable
 import torch
 import torch.distributed as dist
 
+from . import _lib as _abi
+
 
 def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
     """[start, stop) of rank's contiguous row panel; the first M % world ranks get one extra row."""
@@ -242,8 +244,8 @@ class PeerBroadcast:
     so an NCCL broadcast queued beside a GEMM only runs between GEMMs (B200,
     2 GPUs, 32 MiB of B per 4096^3 step: broadcast then GEMM 156 us a step,
     NCCL on a side stream 119 us, copy engines 100 us against 95 us for the
-    GEMM alone).  Here every rank owns two IPC-mapped receive slots (step s
-    uses slot s % 2) and a small flag array; rank 0 scatters piece q-1 of the
+    GEMM alone).  Here every rank owns three IPC-mapped receive slots (step s
+    uses slot s % 3) and a small flag array; rank 0 scatters piece q-1 of the
     buffer to rank q (broadcast_chunks), and each receiving rank forwards its
     piece to the other receivers as soon as it has landed, so every byte
     crosses rank 0's links once.  Copies go into the peers' slots on the copy
@@ -255,18 +257,20 @@ class PeerBroadcast:
     This class allocates and maps the buffers and exchanges their handles.
 
     Per step s, on every rank, in the same order:
-        pb.issue(s + 1, src)      # rank 0: the next step's buffer (others: None)
+        pb.issue(s + 2, src)      # rank 0: the buffer two steps on (others: None)
         pb.wait(s, stream)        # the slot of step s has arrived (no-op on rank 0)
         ... GEMM reading pb.data(s, src) on `stream` ...
-        pb.release(s, stream)     # this rank is done reading slot s % 2
-    with pb.issue(0, src) once before the first step.  Steps count up from 0
+        pb.release(s, stream)     # this rank is done reading slot s % 3
+    with pb.issue(0, src) and pb.issue(1, src) once before the first step (an
+    issue may run at most two steps ahead of the oldest unreleased step: the
+    writers of step s wait for the release of step s - 3).  Steps count up from 0
     and are never reused (flags compare step numbers).  Rank 0 reads `src`
     in place; it must not change until the copies of that step are done
     (pb.copied(s) is an event for that).  Every rank of `group` constructs,
     steps and closes it together; a rank that stops stepping leaves the
     others' streams waiting on its flags (stream waits have no time limit)."""
 
-    SLOTS = 2
+    SLOTS = _abi.B200_BCAST_SLOTS
 
     def __init__(self, nbytes: int, group=None, device=None):
         import ctypes
@@ -363,7 +367,7 @@ class PeerBroadcast:
         return torch.as_tensor(_DevBuf(p, ((self.nbytes + 1) // 2,)), device=self.device).view(torch.uint8)[:self.nbytes]
 
     def release(self, step: int, stream) -> None:
-        """After the work on `stream` that reads slot `step` % 2: tell every
+        """After the work on `stream` that reads the slot of `step`: tell every
         rank that writes into this rank's slots that it may overwrite it."""
         import ctypes
         self._check(self._lib.b200_bcast_release(self._h, step, ctypes.c_void_p(stream.cuda_stream)),

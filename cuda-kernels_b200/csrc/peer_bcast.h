@@ -5,11 +5,17 @@
 
 #include <cuda_runtime.h>
 
+#include "b200_gemm.h"
+
 #include <cstddef>
 #include <cstdint>
 
 namespace b200 {
-constexpr int kBcastSlots = 2;
+// Receive slots per rank (B200_BCAST_SLOTS): with three, the exchange of
+// step s + 2 can run while the GEMM of step s reads its slot, so an exchange
+// slower than one GEMM (8 GPUs: ~124 us against ~97) still stays hidden.
+constexpr int kBcastSlots = B200_BCAST_SLOTS;
+static_assert(kBcastSlots >= 2, "the exchange needs at least two receive slots");
 constexpr int kBcastMaxWorld = 8;
 // Each piece moves in this many parts, and a receiving rank forwards a part
 // as soon as it has landed, so forwarding overlaps rank 0's sending.  With one

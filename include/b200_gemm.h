@@ -153,25 +153,29 @@ B200_API int b200_wait_u32(const void* flag, uint32_t value, void* stream);
 /*
  * Per-step broadcast of one buffer from rank 0 to every rank, built on the
  * three calls above (the multi-GPU driver's B exchange; one process per GPU,
- * world <= 8).  Every rank owns two receive slots of `nbytes` (step s uses
- * slot s % 2) and a flag array of b200_bcast_flag_bytes(world) bytes, zeroed
+ * world <= 8).  Every rank owns B200_BCAST_SLOTS receive slots of `nbytes`
+ * (step s uses slot s % B200_BCAST_SLOTS, so up to two steps can be in flight
+ * ahead of the one being read) and a flag array of
+ * b200_bcast_flag_bytes(world) bytes, zeroed
  * before first use; all of them are mapped in every process (b200_ipc_*).
  * Rank 0 sends piece q-1 (b200_bcast_piece: world-1 pieces, 256-byte
  * aligned) to rank q, and rank q forwards its piece to the other receiving
  * ranks once it has landed, so every byte leaves rank 0 once.
- *   b200_bcast_create   slots[r * 2 + k] = rank r's slot k and flags[r] =
+ *   b200_bcast_create   slots[r * B200_BCAST_SLOTS + k] = rank r's slot k and flags[r] =
  *                       rank r's flags, as mapped in this process.
  *   b200_bcast_issue    queue step `step`'s copies on `stream` (rank 0 from
  *                       `src`; the others forward); every rank calls it.
  *   b200_bcast_wait     `stream` waits until this rank's slot of `step` is
  *                       complete (no-op on rank 0, which reads src).
  *   b200_bcast_release  after the work on `stream` that reads the slot of
- *                       `step`: its writers may overwrite it two steps on.
+ *                       `step`: its writers may overwrite it B200_BCAST_SLOTS
+ *                       steps on.
  * Steps count up from 0 on every rank, each call made by every rank in the
  * same order.  No SMs are used.  A rank that stops calling leaves the
  * others' streams waiting (no time limit, see b200_wait_u32).
  * No reference counterpart: the reference has no multi-GPU code.
  */
+#define B200_BCAST_SLOTS 3
 typedef struct b200_bcast b200_bcast;
 B200_API int b200_bcast_piece(int world, size_t nbytes, int index, size_t* offset, size_t* length);
 B200_API size_t b200_bcast_flag_bytes(int world);

@@ -178,4 +178,4 @@ def test_bcast_pieces_match_the_documented_layout():
             assert got == broadcast_chunks(nbytes, world)
     off, n = ctypes.c_size_t(), ctypes.c_size_t()
     assert lib.b200_bcast_piece(1, 100, 0, ctypes.byref(off), ctypes.byref(n)) == _lib.B200_ERR_INVALID_ARG
-    assert lib.b200_bcast_flag_bytes(8) == 4 * (2 * 8 * 1 + 8 + 1)
+    assert lib.b200_bcast_flag_bytes(8) == 4 * (_lib.B200_BCAST_SLOTS * 8 * 1 + 8 + 1)
