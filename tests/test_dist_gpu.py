@@ -120,7 +120,7 @@ def test_gemm_with_fused_allgather(tmp_path, layout):
             assert torch.equal(per_rank[r][step], c0), f"rank {r} gathered a different C at step {step}"
 
 
-def _peer_bcast_worker(rank, world, port, nbytes, steps, result_dir):
+def _peer_bcast_worker(rank, world, port, nbytes, steps, ahead, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     from datetime import timedelta
     import torch.distributed as dist
@@ -138,12 +138,13 @@ def _peer_bcast_worker(rank, world, port, nbytes, steps, result_dir):
 
         pb = PeerBroadcast(nbytes)
         stream = torch.cuda.current_stream(dev)
-        srcs = [payload(s) for s in range(steps + 1)] if rank == 0 else None
-        pb.issue(0, srcs[0] if rank == 0 else None)
+        srcs = [payload(s) for s in range(steps + ahead)] if rank == 0 else None
+        for s in range(ahead):
+            pb.issue(s, srcs[s] if rank == 0 else None)
         ok = True
         K, N = 256, 1024  # B [K, N] read from the front of each step's buffer
         for s in range(steps):
-            pb.issue(s + 1, srcs[s + 1] if rank == 0 else None)
+            pb.issue(s + ahead, srcs[s + ahead] if rank == 0 else None)
             ref_b = payload(s)[:K * N * 2].view(torch.bfloat16).view(K, N)
             src_b = srcs[s][:K * N * 2].view(torch.bfloat16).view(K, N) if rank == 0 else None
             if s % 3 == 0:
@@ -174,10 +175,12 @@ def _peer_bcast_worker(rank, world, port, nbytes, steps, result_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("ahead", [1, 2])
 @pytest.mark.parametrize("nbytes", [(2 << 20) + 258, 32 << 20])
-def test_peer_broadcast_delivers_every_step(tmp_path, nbytes):
+def test_peer_broadcast_delivers_every_step(tmp_path, nbytes, ahead):
     """PeerBroadcast (copy engines + stream-ordered flags): over several steps,
-    with two receive slots reused in turn, every rank receives exactly the
+    with the three receive slots reused in turn and the copies issued one or
+    two steps ahead of the step being read, every rank receives exactly the
     bytes rank 0 sent for that step, and a GEMM reading them sees them — after
     an explicit wait, and through b200_bcast_gemm, which waits and releases
     inside the CTA-pair kernel or with stream operations around the others."""
@@ -185,7 +188,7 @@ def test_peer_broadcast_delivers_every_step(tmp_path, nbytes):
     if world < 2:
         pytest.skip("needs at least 2 GPUs")
     world = min(world, 8)
-    spawn_ranks(_peer_bcast_worker, lambda port: (world, port, nbytes, 7, str(tmp_path)), world)
+    spawn_ranks(_peer_bcast_worker, lambda port: (world, port, nbytes, 7, ahead, str(tmp_path)), world)
     assert torch.load(os.path.join(tmp_path, "ok.pt"))
 
 
