@@ -326,7 +326,11 @@ class PeerBroadcast:
             raise _lib.B200GemmError(rc, "b200_bcast_create")
         self._h = handle
         self.slot_ptr = own[:self.SLOTS]
-        self.comm = torch.cuda.Stream(self.device)
+        # Steps alternate between two copy streams: the copies of step s+1
+        # need not wait for the last copies of step s (rank 0's pieces of s+1
+        # go out while the others still forward the pieces of s).  Each
+        # step's copies are joined back into its stream.
+        self.comms = [torch.cuda.Stream(self.device) for _ in range(2)]
         self._copied = [torch.cuda.Event() for _ in range(self.SLOTS)]
         dist.barrier(group=group)  # every rank's flags are zero before anyone signals
 
@@ -350,9 +354,10 @@ class PeerBroadcast:
                 raise ValueError("rank 0 needs a contiguous source tensor of nbytes")
             ptr = src.data_ptr()
         self._check(self._lib.b200_bcast_issue_range(self._h, step, ctypes.c_void_p(ptr), offset, length,
-                                                     ctypes.c_void_p(self.comm.cuda_stream)), "b200_bcast_issue")
+                                                     ctypes.c_void_p(self.comms[step % 2].cuda_stream)),
+                    "b200_bcast_issue")
         if self.rank == 0:
-            self._copied[step % self.SLOTS].record(self.comm)
+            self._copied[step % self.SLOTS].record(self.comms[step % 2])
 
     def wait(self, step: int, stream) -> None:
         """Make `stream` wait until this rank's slot of `step` is complete."""
